@@ -1,0 +1,468 @@
+#!/usr/bin/env python3
+"""Benchmark: one LOSSLESS packed-Ulysses DiT block forward at the 480p-5s shape.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl h3b|reference] [--config 480p-5s]
+    torchrun --nproc-per-node N bench.py --gpus N ...          (N > 1: one rank per GPU, NCCL)
+
+A step is one block forward over the whole joint sequence (S = 49,920 video + 1,280
+audio tokens, d=3072, 24x128 heads, FFN 12,288 GELU-tanh, bf16), split into W
+contiguous row shards (Ulysses SP=W; strong scaling: total work fixed). Inputs are
+resident in HBM; each step is timed alone with CUDA events on the compute stream and
+L2 is flushed (256 MiB write) between steps. ms_per_step is the max over ranks.
+
+``e2e`` repeats the step through the same public API with the hidden states copied
+from pinned host memory before and the block output copied back after, inside the
+timed region. ``roofline`` covers the dominant kernel (attention) from CUDA events
+around its launches inside the timed steps. ``cpu_baseline`` times the CPU oracle
+port of the reference path (two gloo ranks) on the BASELINE CPU configuration.
+
+``--impl reference`` times that CPU port as the reference arm (rank 0 only).
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import re
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+METRIC = "DiT block fwd ms at S=49,920 (480p-5s) on 1/2/4/8 B200; a2a GB/s vs NVLink"
+L2_FLUSH_BYTES = 256 << 20
+
+
+def _peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return {"hbm_gbs": data["hbm_gbs"], "bf16_tflops": data["bf16_tflops"],
+                "bf16_tflops_sustained": data.get("bf16_tflops_sustained", data["bf16_tflops"]),
+                "source": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0, "source": "fallback"}
+
+
+def _profile_traffic(hl: int, seq: int) -> float | None:
+    """DRAM bytes per attention launch from the committed ncu summary, scaled from the
+    captured case to this launch by heads (traffic is per (head, sequence) unit)."""
+
+    path = ROOT / "profiles" / "attention_480p5s_sp8.md"
+    if not path.exists():
+        return None
+    m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)\s+at\s+hl=(\d+)\s+S=(\d+)", path.read_text())
+    if not m:
+        return None
+    bytes_, cap_hl, cap_s = float(m.group(1)), int(m.group(2)), int(m.group(3))
+    if cap_s != seq:
+        return None
+    return bytes_ * hl / cap_hl
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+    REASONS = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+
+    def __init__(self, gpus: list[int]) -> None:
+        self.gpus = set(gpus)
+        self.samples: list[tuple[float, float, list[str]]] = []
+        self.proc = None
+        self.thread = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                index = int(parts[0])
+                if index not in self.gpus:
+                    continue
+                sm, sm_max = float(parts[1]), float(parts[2])
+            except ValueError:
+                continue
+            active = [name for name, value in zip(self.REASONS, parts[4:8]) if value.lower() == "active"]
+            self.samples.append((sm, sm_max, active))
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread is not None:
+            self.thread.join(timeout=5)
+        if not self.samples:
+            return None
+        loaded = [s for s in self.samples if s[0] > 0.5 * s[1]] or self.samples
+        reasons = sorted({r for s in self.samples for r in s[2]})
+        return {"sm_mhz": statistics.median(s[0] for s in loaded), "sm_max_mhz": max(s[1] for s in self.samples),
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# CPU reference port (oracle) — the cpu_baseline leg and the --impl reference arm
+# ---------------------------------------------------------------------------
+
+
+def _cpu_worker(rank, world, port, threads, steps, warmup, queue):
+    import torch.distributed as dist
+
+    from h3_flash_b200.runtime.h3_block import H3TransformerBlock
+    from h3_flash_b200.workloads import CONFIGS, adaln_indices, init_block_, positions, rope_tables, split_bounds
+    from oracle.block_ref import block_forward, fp32_params
+
+    torch.set_num_threads(threads)
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=600))
+    cfg = CONFIGS["cpu-gloo"]
+    block = init_block_(H3TransformerBlock(cfg.dim, cfg.heads, cfg.head_dim, cfg.ffn_inner), seed=0)
+    params = fp32_params(block)
+    del block
+    start, stop = split_bounds(cfg.seq, world, rank)
+    g = torch.Generator().manual_seed(1 + start)
+    hidden = torch.randn(stop - start, cfg.dim, generator=g)
+    idx = adaln_indices(cfg)[start:stop]
+    cos, sin = rope_tables(positions(cfg), cfg.rotary_dim, cfg.theta)
+    cos, sin = cos[start:stop], sin[start:stop]
+    kw = dict(heads=cfg.heads, head_dim=cfg.head_dim, eps=cfg.eps, qk_eps=cfg.eps, group=dist.group.WORLD)
+    for _ in range(warmup):
+        block_forward(params, hidden, idx, cos, sin, **kw)
+    results = []
+    for _ in range(steps):
+        timings: dict = {}
+        dist.barrier()
+        t0 = time.perf_counter()
+        block_forward(params, hidden, idx, cos, sin, timings=timings, **kw)
+        dist.barrier()
+        results.append((time.perf_counter() - t0, timings["attention_s"], timings["other_s"]))
+    queue.put((rank, results))
+    dist.destroy_process_group()
+
+
+def cpu_reference_block(steps: int, warmup: int, target_seq: int) -> dict:
+    """Times the oracle block on BASELINE config 1 (S=4,352, W=2 gloo, fp32) and scales each
+    step to ``target_seq`` tokens: attention ~ S^2, everything else ~ S."""
+
+    import socket
+
+    import torch.multiprocessing as mp
+
+    from h3_flash_b200.workloads import CONFIGS
+
+    cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    world = 2
+    threads = max(1, cores // world)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    procs = [ctx.Process(target=_cpu_worker, args=(r, world, port, threads, steps, warmup, queue))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    per_rank = {}
+    for _ in procs:
+        rank, res = queue.get(timeout=3600)
+        per_rank[rank] = res
+    for p in procs:
+        p.join(timeout=60)
+    seq = CONFIGS["cpu-gloo"].seq
+    ratio = target_seq / seq
+    measured, scaled = [], []
+    for i in range(steps):
+        wall = max(per_rank[r][i][0] for r in per_rank)
+        attn = max(per_rank[r][i][1] for r in per_rank)
+        other = max(wall - attn, 0.0)
+        measured.append(wall * 1e3)
+        scaled.append((attn * ratio * ratio + other * ratio) * 1e3)
+    return {
+        "value": statistics.mean(scaled),
+        "unit": "ms",
+        "cores": threads * world,
+        "kind": "port",
+        "measured_ms_at_sample": statistics.mean(measured),
+        "sample": (f"oracle fp32 block (reference path restated: packed-Ulysses a2a over gloo), BASELINE config 1: "
+                   f"S={seq} (4096 video + 256 audio), W={world} gloo ranks x {threads} threads, d=3072, 24x128, "
+                   f"FFN 12288 GELU-tanh; per-step wall time split into attention (scaled by (S/{seq})^2) and "
+                   f"the rest (scaled by S/{seq}) to S={target_seq}"),
+    }
+
+
+# ---------------------------------------------------------------------------
+# GPU block benchmark
+# ---------------------------------------------------------------------------
+
+
+def _dist_setup(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}: launch N>1 under torchrun")
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    return rank, world, local
+
+
+def _barrier(world: int) -> None:
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def _max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def run_h3b(args) -> dict | None:
+    from h3_flash_b200 import _lib
+    from h3_flash_b200.runtime.h3_block import H3BlockStack, H3TransformerBlock
+    from h3_flash_b200.runtime.kernels import install_transformer_fusions
+    from h3_flash_b200.runtime.timing import TIMER
+    from h3_flash_b200.workloads import CONFIGS, adaln_indices, init_block_, positions, rope_tables, split_bounds
+
+    rank, world, local = _dist_setup(args.gpus)
+    cfg = CONFIGS[args.config]
+    if cfg.heads % world:
+        raise SystemExit(f"{cfg.heads} heads do not split over {world} ranks")
+    torch.manual_seed(0)
+    block = init_block_(H3TransformerBlock(cfg.dim, cfg.heads, cfg.head_dim, cfg.ffn_inner, eps=cfg.eps,
+                                           qk_eps=cfg.eps), seed=0)
+    block = block.to(device="cuda", dtype=torch.bfloat16).eval()
+    stack = H3BlockStack([block])
+    install_transformer_fusions(stack)
+    runtime = None
+    if world > 1:
+        from h3_flash_b200.runtime.parallel import install_packed_ulysses
+
+        runtime = install_packed_ulysses(stack)
+        runtime.begin_request()
+    start, stop = split_bounds(cfg.seq, world, rank)
+    rows = stop - start
+    g = torch.Generator().manual_seed(1 + start)
+    hidden_host = torch.randn(1, rows, cfg.dim, generator=g).to(torch.bfloat16).pin_memory()
+    hidden = hidden_host.cuda()
+    idx = adaln_indices(cfg)[start:stop].cuda()
+    cos, sin = rope_tables(positions(cfg), cfg.rotary_dim, cfg.theta)
+    rotary = (cos[start:stop].cuda(), sin[start:stop].cuda())
+    out_host = torch.empty_like(hidden_host).pin_memory()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream()
+
+    def step(x):
+        with torch.no_grad():
+            return stack(x, None, idx, rotary)
+
+    for _ in range(args.warmup):
+        step(hidden)
+    torch.cuda.synchronize()
+
+    sampler = ClockSampler(list(range(world))) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    # ---- device-resident timed steps ----
+    _lib.reset_launch_count()
+    TIMER.reset()
+    TIMER.enabled = True
+    events = []
+    _barrier(world)
+    torch.cuda.synchronize()
+    for _ in range(args.steps):
+        flush.fill_(1)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        step(hidden)
+        e.record(stream)
+        events.append((s, e))
+    torch.cuda.synchronize()
+    _barrier(world)
+    TIMER.enabled = False
+    launches = _lib.launch_count()
+    step_ms = [s.elapsed_time(e) for s, e in events]
+    sections = TIMER.milliseconds()
+    # ---- end-to-end through the public API with host buffers ----
+    e2e_events = []
+    _barrier(world)
+    torch.cuda.synchronize()
+    for _ in range(args.steps):
+        flush.fill_(1)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record(stream)
+        x = hidden_host.to("cuda", non_blocking=True)
+        y = step(x)
+        out_host.copy_(y, non_blocking=True)
+        e.record(stream)
+        e2e_events.append((s, e))
+    torch.cuda.synchronize()
+    _barrier(world)
+    clocks = sampler.stop() if sampler else None
+    e2e_ms = [s.elapsed_time(e) for s, e in e2e_events]
+
+    status = _lib.device_status()
+    if status:
+        raise RuntimeError(f"h3b device status {status}: a kernel wait timed out")
+
+    ms_mean = _max_over_ranks(statistics.mean(step_ms), world)
+    e2e_mean = _max_over_ranks(statistics.mean(e2e_ms), world)
+    attn_ms = statistics.mean(sections.get("attention", [float("nan")]))
+    attn_ms_max = _max_over_ranks(attn_ms, world)
+    hl = cfg.heads // world
+    attn_flop = 4.0 * cfg.seq * cfg.seq * hl * cfg.head_dim
+    peaks = _peaks()
+    achieved = attn_flop / (attn_ms_max * 1e-3) / 1e12
+    peak = peaks["bf16_tflops_sustained"]
+    traffic = _profile_traffic(hl, cfg.seq)
+
+    # secondary rooflines: elementwise HBM bytes, all-to-all bytes over NVLink
+    r = rows
+    d = cfg.dim
+    ew_bytes = (2 * r * d * 2            # rmsnorm_modulate: read x, write
+                + 4 * r * d * 2          # residual+rmsnorm+modulate: 2 reads, 2 writes
+                + 2 * r * cfg.ffn_inner * 2  # GELU: read, write
+                + 3 * r * d * 2          # gated residual: 2 reads, 1 write
+                + 2 * 3 * r * d * 2)     # qknorm+rope+pack: read qkv, write packed
+    ew_ms = sum(statistics.mean(v) for k, v in sections.items() if k in ("elementwise", "qknorm_rope_pack"))
+    ew_ms = _max_over_ranks(ew_ms, world)
+    a2a_bytes = (4 * r * d * 2) * (world - 1) / world if world > 1 else 0.0
+    a2a_ms = _max_over_ranks(sum(sections.get("all_to_all", [0.0])) / max(args.steps, 1), world)
+    sections_total = {k: round(sum(v) / args.steps, 4) for k, v in sections.items()}
+
+    if rank != 0:
+        return None
+    result = {
+        "metric": METRIC,
+        "value": round(ms_mean, 4),
+        "unit": "ms",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_mean, 4),
+        "higher_is_better": False,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic: seeded N(0,1) activations, N(0,0.02) weights, N(0,0.1) AdaLN tables, 3D RoPE tables",
+        "config": {
+            "workload": f"{cfg.name} DiT block forward, packed Ulysses SP{world}",
+            "seq": cfg.seq, "video_tokens": cfg.video_tokens, "audio_tokens": cfg.audio_tokens,
+            "dim": cfg.dim, "heads": cfg.heads, "head_dim": cfg.head_dim, "ffn": f"{cfg.ffn_inner} gelu-tanh",
+            "rotary_dim": cfg.rotary_dim, "rows_per_rank": rows, "heads_per_rank": hl,
+            "parallelism": f"ulysses_sp{world}", "l2": "flushed (256 MiB write) between timed steps",
+        },
+        "e2e": {"value": round(e2e_mean, 4), "unit": "ms",
+                "h2d_bytes_per_step": hidden_host.numel() * hidden_host.element_size(),
+                "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
+        "roofline": {
+            "kernel": "h3b attention_fwd (tcgen05)",
+            "bound": "tensor",
+            "achieved": round(achieved, 2),
+            "peak": peak,
+            "unit": "TFLOP/s",
+            "frac": round(achieved / peak, 4),
+            "peak_note": "sustained cuBLAS bf16 of measured (kernel timed inside the block step)"
+            if peaks["source"] == "measured" else "fallback",
+            "frac_of_burst": round(achieved / peaks["bf16_tflops"], 4),
+            "traffic": traffic,
+            "flop_per_launch": attn_flop,
+            "ms_per_launch": round(attn_ms_max, 4),
+        },
+        "rooflines": {
+            "elementwise_hbm": {"bytes_per_step": ew_bytes, "ms": round(ew_ms, 4),
+                                "achieved_gbs": round(ew_bytes / (ew_ms * 1e-3) / 1e9, 1) if ew_ms else None,
+                                "peak_gbs": peaks["hbm_gbs"],
+                                "frac": round(ew_bytes / (ew_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)
+                                if ew_ms else None},
+            "all_to_all_nvlink": {"bytes_sent_per_gpu": a2a_bytes, "ms": round(a2a_ms, 4),
+                                  "achieved_gbs": round(a2a_bytes / (a2a_ms * 1e-3) / 1e9, 1) if a2a_ms else None,
+                                  "nominal_gbs": 900.0,
+                                  "frac": round(a2a_bytes / (a2a_ms * 1e-3) / 1e9 / 900.0, 4) if a2a_ms else None},
+        },
+        "sections_ms_per_step": sections_total,
+        "gpu_launches": launches,
+        "clocks": clocks,
+    }
+    return result
+
+
+def main() -> int:
+    parser = argparse.ArgumentParser(description=__doc__.splitlines()[1])
+    parser.add_argument("--gpus", type=int, default=1)
+    parser.add_argument("--steps", type=int, default=10)
+    parser.add_argument("--warmup", type=int, default=3)
+    parser.add_argument("--impl", choices=["h3b", "reference"], default="h3b")
+    parser.add_argument("--config", default="480p-5s")
+    parser.add_argument("--no-cpu-baseline", action="store_true")
+    args = parser.parse_args()
+    sys.path.insert(0, str(ROOT))
+    from h3_flash_b200.workloads import CONFIGS
+
+    if args.impl == "reference":
+        rank = int(os.environ.get("RANK", "0"))
+        if rank != 0:
+            return 0
+        base = cpu_reference_block(max(args.steps, 1), max(args.warmup, 0) and 1, CONFIGS[args.config].seq)
+        line = {
+            "metric": METRIC, "impl": "reference", "value": round(base["value"], 2), "unit": "ms",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(base["value"], 2), "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"{args.config} DiT block forward (CPU port of the reference path)"},
+            "cpu_baseline": base,
+            "e2e": {"value": round(base["value"], 2), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }
+        print(json.dumps(line), flush=True)
+        return 0
+
+    result = run_h3b(args)
+    if result is not None:
+        if args.gpus == 1 and not args.no_cpu_baseline:
+            result["cpu_baseline"] = cpu_reference_block(2, 1, CONFIGS[args.config].seq)
+        print(json.dumps(result), flush=True)
+    if args.gpus > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

@@ -1,0 +1,690 @@
+// Dense non-causal attention for B200 (sm_100a): tcgen05 MMA with TMEM
+// accumulators, TMA-fed shared-memory operands, fp32 online softmax.
+//
+// One CTA owns two 128-row query tiles of one (batch, head) and streams the
+// whole key/value sequence in 128-row blocks:
+//
+//   warp 8      TMA producer: Q0, Q1 once, then K_j / V_j into separate rings
+//               (3 K stages, 2 V stages, 32 KB each, 128B-swizzled).
+//   warp 9      MMA issuer (one thread): S_t = Q_t K_j^T into TMEM, then
+//               O_t += P_t V_j with P_t read from TMEM (A operand) and V_j from
+//               shared memory (MN-major B operand). Tiles t=0,1 alternate so the
+//               tensor core works on one tile while the other tile's softmax runs.
+//   warps 0-3   softmax of tile 0, warps 4-7 softmax of tile 1: thread i owns
+//               query row i (TMEM lane i). Reads S with tcgen05.ld, keeps the
+//               running max in the log2 domain, writes P (bf16) over S's first 64
+//               TMEM columns, accumulates the row sum in fp32. O is rescaled in
+//               TMEM only when the running max grows by more than 2^8 (P stays
+//               <= 256, exact in the fp32 accumulator), which after the first
+//               blocks is rare.
+//
+// TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
+// A tcgen05.commit tracks every earlier MMA of the issuing thread, so the
+// commit after S_t(j) also certifies that PV_t(j-1) is done: the softmax may
+// touch O_t once it has seen S_t(j).
+//
+// Every mbarrier wait is bounded by a wall-clock limit. On expiry the thread
+// ORs kStatusAttentionTimeout into the library status word, raises the CTA
+// abort flag and unwinds; the other roles see the flag in their own waits, so
+// the CTA frees its TMEM and exits instead of hanging the GPU.
+//
+// Replaces torch SDPA in src/h3_flash/runtime/parallel/packed_ulysses.py:201-209
+// and the FA4 call in src/h3_flash/runtime/attention/dense_fa4.py:74-81.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cmath>
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+
+namespace h3b {
+namespace attn {
+
+constexpr int kBlockM = 128;  // query rows per tile
+constexpr int kBlockN = 128;  // key rows per block
+constexpr int kHeadDim = 128;
+constexpr int kTiles = 2;  // query tiles per CTA
+constexpr int kKStages = 3;
+constexpr int kVStages = 2;
+constexpr int kThreads = 320;  // 8 softmax warps + TMA warp + MMA warp
+constexpr int kLoadWarp = 8;
+constexpr int kMmaWarp = 9;
+
+constexpr uint32_t kTileBytes = kBlockM * kHeadDim * 2;  // 32 KB: two 16 KB swizzled halves
+constexpr uint32_t kHalfBytes = kTileBytes / 2;
+constexpr uint32_t kSmemQ = 0;
+constexpr uint32_t kSmemK = kSmemQ + kTiles * kTileBytes;
+constexpr uint32_t kSmemV = kSmemK + kKStages * kTileBytes;
+constexpr uint32_t kSmemBar = kSmemV + kVStages * kTileBytes;
+// barriers: q[2], kfull[3], kempty[3], vfull[2], vempty[2], s[2], p[2], o[2] + tmem slot + abort
+constexpr uint32_t kNumBars = kTiles + 2 * kKStages + 2 * kVStages + 3 * kTiles;
+constexpr uint32_t kSmemBytes = kSmemBar + kNumBars * 8 + 16;
+constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;  // slack to 1024-align the base
+
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemS = 0;    // + t*128
+constexpr uint32_t kTmemO = 256;  // + t*128
+
+constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
+
+// Rescale O only when the running row max (log2 units) grew by more than this.
+constexpr float kRescaleThreshold = 8.0f;
+
+// ---------------------------------------------------------------------------
+// PTX wrappers
+// ---------------------------------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ unsigned long long globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity. Returns false if the CTA
+// aborted (another thread timed out) or this wait itself timed out.
+__device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity,
+                                         volatile uint32_t* abort_flag, unsigned int* status) {
+  if (mbar_try(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try(bar, parity)) return true;
+    if ((i & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > kWaitLimitNs) {
+        *abort_flag = 1u;
+        if (status) atomicOr(status, kStatusAttentionTimeout);
+        return false;
+      }
+    }
+  }
+}
+
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Shared-memory matrix descriptor, 128B swizzle, sm_100 version field.
+__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;  // descriptor version (sm_100)
+  d |= (uint64_t)2 << 61;  // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: bf16 x bf16 -> f32, M=128, N=128.
+// b_mn_major selects an MN-major B operand (V in P.V).
+__host__ __device__ constexpr uint32_t instr_desc(bool b_mn_major) {
+  return (1u << 4)                   // D format f32
+         | (1u << 7)                 // A bf16
+         | (1u << 10)                // B bf16
+         | ((b_mn_major ? 1u : 0u) << 16)
+         | ((uint32_t)(kBlockN >> 3) << 17)  // N >> 3
+         | ((uint32_t)(kBlockM >> 4) << 24); // M >> 4
+}
+
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                       uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void mma_commit(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      : "memory");
+}
+
+// 32 lanes x 32 consecutive 32-bit TMEM columns -> 32 registers per thread.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+      "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]),
+        "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]),
+        "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+
+// Waits for this thread's outstanding tcgen05.ld and pins the 32 registers
+// after the wait so no use is scheduled above it.
+__device__ __forceinline__ void tmem_ld_wait(uint32_t (&r)[32]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]));
+  asm volatile(""
+               : "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]),
+                 "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]),
+                 "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]),
+                 "+r"(r[31]));
+}
+__device__ __forceinline__ void tmem_pin(uint32_t (&r)[32]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]));
+  asm volatile(""
+               : "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]),
+                 "+r"(r[21]), "+r"(r[22]), "+r"(r[23]), "+r"(r[24]), "+r"(r[25]),
+                 "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]), "+r"(r[30]),
+                 "+r"(r[31]));
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]),
+      "r"(r[15]), "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]),
+      "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]),
+      "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ float ex2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// ---------------------------------------------------------------------------
+// Kernel
+// ---------------------------------------------------------------------------
+
+struct Params {
+  __nv_bfloat16* out;
+  int64_t o_batch_stride, o_row_stride, o_head_stride;
+  int seq_q, seq_k;
+  float scale_log2;  // softmax_scale * log2(e)
+  unsigned int* status;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    attention_fwd(const __grid_constant__ CUtensorMap q_map,
+                  const __grid_constant__ CUtensorMap k_map,
+                  const __grid_constant__ CUtensorMap v_map, const Params prm) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t sQ = sbase + kSmemQ;
+  const uint32_t sK = sbase + kSmemK;
+  const uint32_t sV = sbase + kSmemV;
+  const uint32_t bars = sbase + kSmemBar;
+  auto bar_q = [&](int t) { return bars + 8u * t; };
+  auto bar_kfull = [&](int s) { return bars + 8u * (kTiles + s); };
+  auto bar_kempty = [&](int s) { return bars + 8u * (kTiles + kKStages + s); };
+  auto bar_vfull = [&](int s) { return bars + 8u * (kTiles + 2 * kKStages + s); };
+  auto bar_vempty = [&](int s) { return bars + 8u * (kTiles + 2 * kKStages + kVStages + s); };
+  auto bar_s = [&](int t) { return bars + 8u * (kTiles + 2 * kKStages + 2 * kVStages + t); };
+  auto bar_p = [&](int t) {
+    return bars + 8u * (kTiles + 2 * kKStages + 2 * kVStages + kTiles + t);
+  };
+  auto bar_o = [&](int t) {
+    return bars + 8u * (kTiles + 2 * kKStages + 2 * kVStages + 2 * kTiles + t);
+  };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemBar + kNumBars * 8);
+  volatile uint32_t* abort_flag = tmem_slot + 1;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int head = blockIdx.y;
+  const int batch = blockIdx.z;
+  const int q_row0 = blockIdx.x * (kTiles * kBlockM);
+  const int n_kv = (prm.seq_k + kBlockN - 1) / kBlockN;
+
+  if (threadIdx.x == 0) {
+    for (int t = 0; t < kTiles; ++t) {
+      mbar_init(bar_q(t), 1);
+      mbar_init(bar_s(t), 1);
+      mbar_init(bar_p(t), 128);
+      mbar_init(bar_o(t), 1);
+    }
+    for (int s = 0; s < kKStages; ++s) {
+      mbar_init(bar_kfull(s), 1);
+      mbar_init(bar_kempty(s), 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
+      mbar_init(bar_vfull(s), 1);
+      mbar_init(bar_vempty(s), 1);
+    }
+    *abort_flag = 0u;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == kMmaWarp) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                     smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  if (warp == kLoadWarp && lane == 0) {
+    prefetch_map(&q_map);
+    prefetch_map(&k_map);
+    prefetch_map(&v_map);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == kLoadWarp) {
+    if (lane == 0) {
+      // ---------------- TMA producer ----------------
+      bool ok = true;
+      for (int t = 0; t < kTiles; ++t) {
+        mbar_expect_tx(bar_q(t), kTileBytes);
+        const uint32_t dst = sQ + t * kTileBytes;
+        const int row = q_row0 + t * kBlockM;
+        tma_load_4d(dst, &q_map, bar_q(t), 0, head, row, batch);
+        tma_load_4d(dst + kHalfBytes, &q_map, bar_q(t), 64, head, row, batch);
+      }
+      for (int j = 0; j < n_kv && ok; ++j) {
+        const int ks = j % kKStages, vs = j % kVStages;
+        ok = wait_bar(bar_kempty(ks), ((j / kKStages) & 1) ^ 1, abort_flag, prm.status);
+        if (!ok) break;
+        mbar_expect_tx(bar_kfull(ks), kTileBytes);
+        const uint32_t kdst = sK + ks * kTileBytes;
+        tma_load_4d(kdst, &k_map, bar_kfull(ks), 0, head, j * kBlockN, batch);
+        tma_load_4d(kdst + kHalfBytes, &k_map, bar_kfull(ks), 64, head, j * kBlockN, batch);
+        ok = wait_bar(bar_vempty(vs), ((j / kVStages) & 1) ^ 1, abort_flag, prm.status);
+        if (!ok) break;
+        mbar_expect_tx(bar_vfull(vs), kTileBytes);
+        const uint32_t vdst = sV + vs * kTileBytes;
+        tma_load_4d(vdst, &v_map, bar_vfull(vs), 0, head, j * kBlockN, batch);
+        tma_load_4d(vdst + kHalfBytes, &v_map, bar_vfull(vs), 64, head, j * kBlockN, batch);
+      }
+    }
+  } else if (warp == kMmaWarp) {
+    if (lane == 0) {
+      // ---------------- MMA issuer ----------------
+      constexpr uint32_t idesc_qk = instr_desc(false);
+      constexpr uint32_t idesc_pv = instr_desc(true);
+      bool ok = true;
+      for (int t = 0; t < kTiles && ok; ++t) ok = wait_bar(bar_q(t), 0, abort_flag, prm.status);
+      // S_t = Q_t K_j^T : 8 MMAs of K=16 over the 128 head dims.
+      auto issue_s = [&](int t, int j) {
+        const uint32_t q_base = sQ + t * kTileBytes;
+        const uint32_t k_base = sK + (j % kKStages) * kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kHeadDim / 16; ++kk) {
+          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
+          mma_ss(tmem + kTmemS + t * 128, smem_desc(q_base + off, 16, 1024),
+                 smem_desc(k_base + off, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
+        }
+      };
+      // O_t += P_t V_j : 8 MMAs of K=16 over the 128 keys of the block.
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t v_base = sV + (j % kVStages) * kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kBlockN / 16; ++kk) {
+          mma_ts(tmem + kTmemO + t * 128, tmem + kTmemS + t * 128 + kk * 8,
+                 smem_desc(v_base + kk * 2048, kHalfBytes, 1024), idesc_pv,
+                 (j > 0 || kk > 0) ? 1u : 0u);
+        }
+      };
+      if (ok) ok = wait_bar(bar_kfull(0), 0, abort_flag, prm.status);
+      if (ok) {
+        tc_fence_after();
+        for (int t = 0; t < kTiles; ++t) {
+          issue_s(t, 0);
+          mma_commit(bar_s(t));
+        }
+        mma_commit(bar_kempty(0));
+      }
+      for (int j = 0; j < n_kv && ok; ++j) {
+        for (int t = 0; t < kTiles && ok; ++t) {
+          ok = wait_bar(bar_p(t), j & 1, abort_flag, prm.status);
+          if (!ok) break;
+          if (t == 0) {
+            ok = wait_bar(bar_vfull(j % kVStages), (j / kVStages) & 1, abort_flag, prm.status);
+            if (!ok) break;
+          }
+          tc_fence_after();
+          issue_pv(t, j);
+          if (t == kTiles - 1) mma_commit(bar_vempty(j % kVStages));
+          if (j + 1 < n_kv) {
+            if (t == 0) {
+              ok = wait_bar(bar_kfull((j + 1) % kKStages), ((j + 1) / kKStages) & 1,
+                            abort_flag, prm.status);
+              if (!ok) break;
+              tc_fence_after();
+            }
+            issue_s(t, j + 1);
+            mma_commit(bar_s(t));
+            if (t == kTiles - 1) mma_commit(bar_kempty((j + 1) % kKStages));
+          } else {
+            mma_commit(bar_o(t));
+          }
+        }
+      }
+    }
+  } else {
+    // ---------------- softmax warpgroups ----------------
+    const int t = warp >> 2;                 // query tile of this warpgroup
+    const int lane_base = (warp & 3) * 32;   // TMEM lanes owned by this warp
+    const int row_in_tile = lane_base + lane;
+    const uint32_t t_s = tmem + ((uint32_t)lane_base << 16) + kTmemS + t * 128;
+    const uint32_t t_o = tmem + ((uint32_t)lane_base << 16) + kTmemO + t * 128;
+    const float c = prm.scale_log2;
+    float m_use = -INFINITY;
+    float l_sum = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n_kv; ++j) {
+      ok = wait_bar(bar_s(t), j & 1, abort_flag, prm.status);
+      // tcgen05.ld/st below are warp-collective: leave together or not at all.
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t s[4][32];
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) tmem_ld32(t_s + q4 * 32, s[q4]);
+      tmem_ld_wait(s[0]);
+      tmem_pin(s[1]);
+      tmem_pin(s[2]);
+      tmem_pin(s[3]);
+      const int valid = prm.seq_k - j * kBlockN;  // keys of this block that exist
+      if (valid < kBlockN) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4)
+#pragma unroll
+          for (int i = 0; i < 32; ++i)
+            if (q4 * 32 + i >= valid) s[q4][i] = __float_as_uint(-INFINITY);
+      }
+      // Row max with 8 independent chains (a single chain is latency-bound).
+      float mxp[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mxp[i] = -INFINITY;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4)
+#pragma unroll
+        for (int i = 0; i < 32; ++i) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(s[q4][i]));
+      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+      const float m_new = mx * c;
+      const bool need = m_new > m_use + kRescaleThreshold;
+      // tcgen05.ld/st are warp-collective: the whole warp rescales if any row must.
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // PV_t(j-1) is complete: the S_t(j) commit covers every earlier MMA.
+        const float alpha = need ? ex2(m_use - m_new) : 1.f;
+#pragma unroll 1
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint32_t o[32];
+          tmem_ld32(t_o + q4 * 32, o);
+          tmem_ld_wait(o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(t_o + q4 * 32, o);
+        }
+        l_sum *= alpha;
+      }
+      if (need) m_use = m_new;
+      const float neg_m = -m_use;
+      float lp[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float p0 = ex2(fmaf(__uint_as_float(s[q4][2 * i]), c, neg_m));
+          const float p1 = ex2(fmaf(__uint_as_float(s[q4][2 * i + 1]), c, neg_m));
+          lp[i & 3] += p0 + p1;
+          pk[i] = pack_bf16(p0, p1);
+        }
+        tmem_st16(t_s + q4 * 16, pk);
+      }
+      l_sum += (lp[0] + lp[1]) + (lp[2] + lp[3]);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(bar_p(t));
+    }
+    // ---------------- epilogue: O / l -> bf16 -> global ----------------
+    if (ok) ok = wait_bar(bar_o(t), 0, abort_flag, prm.status);
+    ok = __all_sync(0xffffffffu, ok);
+    if (ok) {
+      tc_fence_after();
+      const int row = q_row0 + t * kBlockM + row_in_tile;
+      const float inv_l = 1.f / l_sum;
+      __nv_bfloat16* dst = prm.out + (int64_t)batch * prm.o_batch_stride +
+                           (int64_t)row * prm.o_row_stride + (int64_t)head * prm.o_head_stride;
+#pragma unroll 1
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t o[32];
+        tmem_ld32(t_o + q4 * 32, o);
+        tmem_ld_wait(o);
+        if (row < prm.seq_q) {
+#pragma unroll
+          for (int v8 = 0; v8 < 4; ++v8) {
+            uint4 u;
+            u.x = pack_bf16(__uint_as_float(o[v8 * 8 + 0]) * inv_l,
+                            __uint_as_float(o[v8 * 8 + 1]) * inv_l);
+            u.y = pack_bf16(__uint_as_float(o[v8 * 8 + 2]) * inv_l,
+                            __uint_as_float(o[v8 * 8 + 3]) * inv_l);
+            u.z = pack_bf16(__uint_as_float(o[v8 * 8 + 4]) * inv_l,
+                            __uint_as_float(o[v8 * 8 + 5]) * inv_l);
+            u.w = pack_bf16(__uint_as_float(o[v8 * 8 + 6]) * inv_l,
+                            __uint_as_float(o[v8 * 8 + 7]) * inv_l);
+            *reinterpret_cast<uint4*>(dst + q4 * 32 + v8 * 8) = u;
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                 "r"(kTmemCols)
+                 : "memory");
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 4-D map over (head_dim, heads, rows, batch) with a (64, 1, 128, 1) box.
+int make_map(CUtensorMap* map, const void* base, int64_t batch, int64_t seq, int64_t heads,
+             int64_t bs, int64_t rs, int64_t hs, const char* name) {
+  auto fn = encode_fn();
+  if (fn == nullptr) {
+    set_error("h3b_attention: cuTensorMapEncodeTiled is unavailable");
+    return H3B_ERR_CUDA;
+  }
+  // Size-1 dimensions never step their stride; give them a valid one.
+  if (heads == 1) hs = kHeadDim;
+  if (batch == 1) bs = rs * (seq > 0 ? seq : 1);
+  cuuint64_t dims[4] = {(cuuint64_t)kHeadDim, (cuuint64_t)heads, (cuuint64_t)seq,
+                        (cuuint64_t)batch};
+  cuuint64_t strides[3] = {(cuuint64_t)hs * 2, (cuuint64_t)rs * 2, (cuuint64_t)bs * 2};
+  cuuint32_t box[4] = {64, 1, (cuuint32_t)kBlockM, 1};
+  cuuint32_t estr[4] = {1, 1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims,
+                  strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[256];
+    snprintf(buf, sizeof(buf), "h3b_attention: tensor map for %s rejected (CUresult %d)", name,
+             (int)r);
+    set_error(buf);
+    return H3B_ERR_CUDA;
+  }
+  return H3B_OK;
+}
+
+}  // namespace attn
+}  // namespace h3b
+
+extern "C" int h3b_attention(void* out, const void* q, const void* k, const void* v,
+                             int64_t batch, int64_t seq_q, int64_t seq_k, int64_t heads,
+                             int64_t head_dim, int64_t q_batch_stride, int64_t q_row_stride,
+                             int64_t q_head_stride, int64_t k_batch_stride,
+                             int64_t k_row_stride, int64_t k_head_stride,
+                             int64_t v_batch_stride, int64_t v_row_stride,
+                             int64_t v_head_stride, int64_t o_batch_stride,
+                             int64_t o_row_stride, int64_t o_head_stride, float softmax_scale,
+                             h3b_stream_t stream) {
+  using namespace h3b::attn;
+  H3B_REQUIRE(batch >= 0 && seq_q >= 0 && seq_k >= 0 && heads >= 0,
+              "attention: negative shape");
+  if (head_dim != kHeadDim) {
+    h3b::set_error("h3b_attention: head_dim must be 128");
+    return H3B_ERR_UNSUPPORTED;
+  }
+  if (batch == 0 || seq_q == 0 || heads == 0) return H3B_OK;
+  H3B_REQUIRE(seq_k > 0, "attention: empty key sequence");
+  H3B_REQUIRE(batch <= 65535 && heads <= 65535 && seq_q < (1LL << 31) && seq_k < (1LL << 31),
+              "attention: shape exceeds launch limits");
+  H3B_REQUIRE(h3b::aligned16(q) && h3b::aligned16(k) && h3b::aligned16(v) &&
+                  h3b::aligned16(out),
+              "attention: q, k, v, out must be 16-byte aligned");
+  const int64_t strides[12] = {q_batch_stride, q_row_stride, q_head_stride, k_batch_stride,
+                               k_row_stride,   k_head_stride, v_batch_stride, v_row_stride,
+                               v_head_stride,  o_batch_stride, o_row_stride, o_head_stride};
+  for (int i = 0; i < 12; ++i) {
+    const bool unit = (i % 3 == 0 && batch == 1) || (i % 3 == 2 && heads == 1);
+    H3B_REQUIRE(unit || (strides[i] % 8 == 0 && strides[i] > 0),
+                "attention: strides must be positive multiples of 8 elements");
+  }
+  CUtensorMap qm, km, vm;
+  int rc;
+  if ((rc = make_map(&qm, q, batch, seq_q, heads, q_batch_stride, q_row_stride, q_head_stride,
+                     "q")) != H3B_OK)
+    return rc;
+  if ((rc = make_map(&km, k, batch, seq_k, heads, k_batch_stride, k_row_stride, k_head_stride,
+                     "k")) != H3B_OK)
+    return rc;
+  if ((rc = make_map(&vm, v, batch, seq_k, heads, v_batch_stride, v_row_stride, v_head_stride,
+                     "v")) != H3B_OK)
+    return rc;
+  {
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(
+          attention_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemAlloc);
+      if (e != cudaSuccess) {
+        h3b::set_error(std::string("h3b_attention: cannot reserve shared memory: ") +
+                       cudaGetErrorString(e));
+        return H3B_ERR_CUDA;
+      }
+      if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    }
+  }
+  Params p;
+  p.out = reinterpret_cast<__nv_bfloat16*>(out);
+  p.o_batch_stride = o_batch_stride;
+  p.o_row_stride = o_row_stride;
+  p.o_head_stride = o_head_stride;
+  p.seq_q = (int)seq_q;
+  p.seq_k = (int)seq_k;
+  p.scale_log2 = (float)((double)softmax_scale * 1.4426950408889634);
+  p.status = h3b::status_ptr();
+  dim3 grid((unsigned)((seq_q + kTiles * kBlockM - 1) / (kTiles * kBlockM)), (unsigned)heads,
+            (unsigned)batch);
+  attention_fwd<<<grid, kThreads, kSmemAlloc, stream>>>(qm, km, vm, p);
+  return h3b::check_launch("h3b_attention");
+}

@@ -1,0 +1,109 @@
+// Shared helpers for the libh3b.so kernels: error plumbing, bf16 packing and
+// 128-bit vector access. sm_100a only.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/h3b.h"
+
+namespace h3b {
+
+// Per-host-thread error string returned by h3b_last_error().
+void set_error(const std::string& msg);
+void clear_error();
+
+// Returns H3B_OK or records the pending launch error and returns H3B_ERR_CUDA.
+int check_launch(const char* what);
+
+// Device address of this device's status word (bit flags documented in
+// h3b.h), or nullptr if it cannot be resolved. Defined in abi.cu.
+unsigned int* status_ptr();
+
+enum : unsigned int { kStatusAttentionTimeout = 1u };
+
+#define H3B_REQUIRE(cond, ...)                                   \
+  do {                                                           \
+    if (!(cond)) {                                               \
+      char _h3b_buf[512];                                        \
+      snprintf(_h3b_buf, sizeof(_h3b_buf), __VA_ARGS__);         \
+      ::h3b::set_error(_h3b_buf);                                \
+      return H3B_ERR_VALUE;                                      \
+    }                                                            \
+  } while (0)
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// ---- bf16 <-> fp32 ---------------------------------------------------------
+
+__device__ __forceinline__ float bf16lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+
+// Round two fp32 values to nearest-even bf16 and pack (lo in bits 0..15).
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+struct f8 {
+  float v[8];
+};
+
+__device__ __forceinline__ f8 unpack8(uint4 u) {
+  f8 r;
+  r.v[0] = bf16lo(u.x); r.v[1] = bf16hi(u.x);
+  r.v[2] = bf16lo(u.y); r.v[3] = bf16hi(u.y);
+  r.v[4] = bf16lo(u.z); r.v[5] = bf16hi(u.z);
+  r.v[6] = bf16lo(u.w); r.v[7] = bf16hi(u.w);
+  return r;
+}
+
+__device__ __forceinline__ uint4 pack8(const float* v) {
+  uint4 u;
+  u.x = pack_bf16(v[0], v[1]);
+  u.y = pack_bf16(v[2], v[3]);
+  u.z = pack_bf16(v[4], v[5]);
+  u.w = pack_bf16(v[6], v[7]);
+  return u;
+}
+
+// Streaming 128-bit accesses for data touched exactly once.
+__device__ __forceinline__ uint4 ld_stream(const void* p) {
+  uint4 r;
+  asm volatile("ld.global.cs.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(p));
+  return r;
+}
+__device__ __forceinline__ void st_stream(void* p, uint4 v) {
+  asm volatile("st.global.cs.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(v.x), "r"(v.y),
+               "r"(v.z), "r"(v.w)
+               : "memory");
+}
+// Cached (L1/L2) read for small tables reused across rows.
+__device__ __forceinline__ uint4 ld_cached(const void* p) {
+  return __ldg(reinterpret_cast<const uint4*>(p));
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+inline int num_sms() {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+  }
+  return sms;
+}
+
+}  // namespace h3b

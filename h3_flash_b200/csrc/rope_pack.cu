@@ -1,0 +1,378 @@
+// Per-head QK RMSNorm + partial rotate-half RoPE, fused with the packed-Ulysses
+// destination-major QKV pack; plus the standalone pack and head-merge relayouts.
+//
+// Head rows of D=128 bf16 are handled by D/8 lanes (16 lanes, two head rows per
+// warp), 16 bytes per lane. The rotate-half partner of column c (c < rot) is
+// c +/- rot/2; when rot/2 is a multiple of 8 the partner chunk sits rot/16 lanes
+// away in the same head row and is fetched with a shuffle, otherwise it is read
+// back from a per-warp shared-memory copy of the normalised row.
+//
+// Semantics: src/h3_flash/runtime/kernels/fusions.py:125-175 (norm + RoPE),
+// src/h3_flash/runtime/parallel/relayout.py:10-67 (pack / merge).
+#include <cstdio>
+
+#include "common.cuh"
+
+namespace h3b {
+namespace {
+
+// Normalise + rope one 8-column chunk owned by this lane. `v` holds the chunk's
+// raw values on entry and the output on exit. All lanes of the warp must call
+// this together (shuffles); `active` marks lanes that own a real chunk.
+template <int D, bool kShufflePartner>
+__device__ __forceinline__ void norm_rope_chunk(float (&v)[8], const __nv_bfloat16* weight,
+                                                const float* cos_row, const float* sin_row,
+                                                int rot, float eps, int sublane,
+                                                float* smem_row) {
+  constexpr int L = D / 8;  // lanes per head row
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+  // Reduce across the L lanes of this head row.
+#pragma unroll
+  for (int o = L / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(ss / (float)D + eps);
+  const int col = sublane * 8;
+  f8 w = unpack8(ld_cached(weight + col));
+  float n[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) n[j] = v[j] * r * w.v[j];
+  if (rot == 0) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = n[j];
+    return;
+  }
+  const int half = rot >> 1;
+  float p[8];
+  if (kShufflePartner) {
+    const int dl = half >> 3;
+    const int lane = threadIdx.x & 31;
+    const int src = (col < half) ? lane + dl : lane - dl;
+    const int src_ok = (col < rot) ? src : lane;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) p[j] = __shfl_sync(0xffffffffu, n[j], src_ok);
+    if (col < rot) {
+      const float sgn = (col < half) ? -1.f : 1.f;
+      const float4 c0 = __ldg(reinterpret_cast<const float4*>(cos_row + col));
+      const float4 c1 = __ldg(reinterpret_cast<const float4*>(cos_row + col + 4));
+      const float4 s0 = __ldg(reinterpret_cast<const float4*>(sin_row + col));
+      const float4 s1 = __ldg(reinterpret_cast<const float4*>(sin_row + col + 4));
+      const float cs[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+      const float sn[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = n[j] * cs[j] + (sgn * p[j]) * sn[j];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = n[j];
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) smem_row[col + j] = n[j];
+    __syncwarp();
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int c = col + j;
+      if (c < rot) {
+        const bool first = c < half;
+        const float pv = smem_row[first ? c + half : c - half];
+        const float rotated = first ? -pv : pv;
+        v[j] = n[j] * __ldg(cos_row + c) + rotated * __ldg(sin_row + c);
+      } else {
+        v[j] = n[j];
+      }
+    }
+    __syncwarp();
+  }
+}
+
+// ---- standalone fused_qknorm_rope: x, out contiguous [B*S*H, D] -------------
+
+template <int D, bool kShuffle>
+__global__ void __launch_bounds__(256) qknorm_rope_kernel(__nv_bfloat16* out,
+                                                         const __nv_bfloat16* x,
+                                                         const __nv_bfloat16* weight,
+                                                         const float* cos, const float* sin,
+                                                         int64_t nrows, int64_t heads,
+                                                         int64_t seq, int rot, float eps) {
+  constexpr int L = D / 8;
+  constexpr int kRowsPerCta = 256 / L;
+  __shared__ float smem[kShuffle ? 1 : kRowsPerCta * D];
+  const int sub = threadIdx.x % L;
+  const int slot = threadIdx.x / L;
+  const int64_t hr = (int64_t)blockIdx.x * kRowsPerCta + slot;
+  const bool active = hr < nrows;
+  const int64_t hr_c = active ? hr : nrows - 1;  // keep every lane in the shuffles
+  const int64_t token = (hr_c / heads) % seq;
+  float v[8];
+  f8 in = unpack8(ld_stream(x + hr_c * D + sub * 8));
+#pragma unroll
+  for (int j = 0; j < 8; ++j) v[j] = in.v[j];
+  norm_rope_chunk<D, kShuffle>(v, weight, cos + token * rot, sin + token * rot, rot, eps, sub,
+                               kShuffle ? nullptr : smem + slot * D);
+  if (active) st_stream(out + hr * D + sub * 8, pack8(v));
+}
+
+// ---- fused q/k norm + rope + destination-major pack -------------------------
+//
+// One CTA per token row. Work items are the 3*H head rows of that token
+// (q heads, k heads, v heads); each group of L lanes takes items slot,
+// slot+G, ... (G = 256/L head rows in flight per CTA pass).
+template <int D, bool kShuffle>
+__global__ void __launch_bounds__(256) qknorm_rope_pack_kernel(
+    __nv_bfloat16* send, const __nv_bfloat16* q, const __nv_bfloat16* k,
+    const __nv_bfloat16* v, int64_t q_stride, int64_t k_stride, int64_t v_stride,
+    const __nv_bfloat16* wq, const __nv_bfloat16* wk, const float* cos, const float* sin,
+    int64_t rows, int heads, int hl, int rot, float q_eps, float k_eps) {
+  constexpr int L = D / 8;
+  constexpr int G = 256 / L;
+  __shared__ float smem[kShuffle ? 1 : G * D];
+  const int sub = threadIdx.x % L;
+  const int slot = threadIdx.x / L;
+  const int64_t row = blockIdx.x;
+  const float* cos_row = cos + row * rot;
+  const float* sin_row = sin + row * rot;
+  const int items = 3 * heads;
+  for (int it0 = 0; it0 < items; it0 += G) {
+    const int it = it0 + slot;
+    const bool active = it < items;
+    const int itc = active ? it : items - 1;
+    const int part = itc / heads;  // 0 = q, 1 = k, 2 = v (uniform per head row)
+    const int g = itc - part * heads;
+    const __nv_bfloat16* src =
+        part == 0 ? q + row * q_stride : (part == 1 ? k + row * k_stride : v + row * v_stride);
+    const uint4 raw = ld_stream(src + (int64_t)g * D + sub * 8);
+    f8 in = unpack8(raw);
+    // Head rows of different parts share a warp: the warp-collective norm runs
+    // for every lane and v rows store their raw bits unchanged.
+    float nv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) nv[j] = in.v[j];
+    norm_rope_chunk<D, kShuffle>(nv, part == 1 ? wk : wq, cos_row, sin_row, rot,
+                                 part == 1 ? k_eps : q_eps, sub,
+                                 kShuffle ? nullptr : smem + slot * D);
+    if (active) {
+      const int dst = g / hl;
+      const int lh = g - dst * hl;
+      __nv_bfloat16* o =
+          send + (((int64_t)dst * rows + row) * hl + lh) * (3 * D) + part * D + sub * 8;
+      st_stream(o, part == 2 ? raw : pack8(nv));
+    }
+  }
+}
+
+// ---- pack_qkv_destination_major (no arithmetic) ----------------------------
+
+template <int D>
+__global__ void __launch_bounds__(256) pack_qkv_kernel(
+    __nv_bfloat16* out, const __nv_bfloat16* q, const __nv_bfloat16* k,
+    const __nv_bfloat16* v, int64_t rows, int heads, int hl, int64_t qr, int64_t qh,
+    int64_t kr, int64_t kh, int64_t vr, int64_t vh) {
+  constexpr int C = D / 8;  // chunks per head row
+  const int64_t row = blockIdx.x;
+  const int per_row = heads * 3 * C;
+  for (int j = threadIdx.x; j < per_row; j += 256) {
+    const int c = j % C;
+    const int t = j / C;
+    const int part = t % 3;
+    const int g = t / 3;
+    const __nv_bfloat16* src = part == 0   ? q + row * qr + g * qh
+                               : part == 1 ? k + row * kr + g * kh
+                                           : v + row * vr + g * vh;
+    const int dst = g / hl, lh = g - dst * hl;
+    __nv_bfloat16* o = out + (((int64_t)dst * rows + row) * hl + lh) * (3 * D) + part * D;
+    st_stream(o + c * 8, ld_stream(src + c * 8));
+  }
+}
+
+// Generic scalar pack for strides / widths the vector kernel cannot address.
+__global__ void pack_qkv_scalar(__nv_bfloat16* out, const __nv_bfloat16* q,
+                                const __nv_bfloat16* k, const __nv_bfloat16* v, int64_t rows,
+                                int64_t heads, int64_t hl, int64_t D, int64_t qr, int64_t qh,
+                                int64_t kr, int64_t kh, int64_t vr, int64_t vh) {
+  const int64_t total = rows * heads * D;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t d = i % D;
+    const int64_t slot = i / D;
+    const int64_t lh = slot % hl;
+    const int64_t rs = slot / hl;
+    const int64_t row = rs % rows;
+    const int64_t dst = rs / rows;
+    const int64_t g = dst * hl + lh;
+    const int64_t base = slot * 3 * D + d;
+    out[base] = q[row * qr + g * qh + d];
+    out[base + D] = k[row * kr + g * kh + d];
+    out[base + 2 * D] = v[row * vr + g * vh + d];
+  }
+}
+
+// ---- merge_heads: out[row, src, :] = x[src, row, :] ------------------------
+
+__global__ void __launch_bounds__(256) merge_heads_vec(__nv_bfloat16* out,
+                                                      const __nv_bfloat16* x, int64_t world,
+                                                      int64_t rows, int64_t inner8) {
+  // One CTA per output row: copies world * inner contiguous output values.
+  const int64_t row = blockIdx.x;
+  const int64_t per_row = world * inner8;
+  for (int64_t j = threadIdx.x; j < per_row; j += 256) {
+    const int64_t src = j / inner8;
+    const int64_t c = j - src * inner8;
+    st_stream(out + (row * per_row + j) * 8, ld_stream(x + ((src * rows + row) * inner8 + c) * 8));
+  }
+}
+
+__global__ void merge_heads_scalar(__nv_bfloat16* out, const __nv_bfloat16* x, int64_t world,
+                                   int64_t rows, int64_t inner) {
+  const int64_t total = world * rows * inner;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t tail = i % inner;
+    const int64_t slot = i / inner;
+    const int64_t src = slot % world;
+    const int64_t row = slot / world;
+    out[i] = x[(src * rows + row) * inner + tail];
+  }
+}
+
+template <int D, bool kShuffle>
+void launch_qkrope(__nv_bfloat16* out, const __nv_bfloat16* x, const __nv_bfloat16* w,
+                   const float* cos, const float* sin, int64_t nrows, int64_t heads,
+                   int64_t seq, int rot, float eps, cudaStream_t s) {
+  constexpr int kRowsPerCta = 256 / (D / 8);
+  const int64_t grid = (nrows + kRowsPerCta - 1) / kRowsPerCta;
+  qknorm_rope_kernel<D, kShuffle><<<(unsigned)grid, 256, 0, s>>>(out, x, w, cos, sin, nrows,
+                                                                 heads, seq, rot, eps);
+}
+
+}  // namespace
+}  // namespace h3b
+
+using h3b::aligned16;
+
+extern "C" int h3b_qknorm_rope(void* out, const void* x, const void* weight, const float* cos,
+                               const float* sin, int64_t batch, int64_t seq, int64_t heads,
+                               int64_t head_dim, int64_t rotary_dim, float eps,
+                               h3b_stream_t stream) {
+  H3B_REQUIRE(batch >= 0 && seq >= 0 && heads >= 0, "qknorm_rope: negative shape");
+  H3B_REQUIRE(rotary_dim >= 0 && rotary_dim <= head_dim && rotary_dim % 2 == 0,
+              "fused qknorm+rope requires an even rotary dimension no wider than the head, "
+              "got rotary_dim=%lld, head_dim=%lld",
+              (long long)rotary_dim, (long long)head_dim);
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256) {
+    h3b::set_error("qknorm_rope: head_dim must be 64, 128 or 256");
+    return H3B_ERR_UNSUPPORTED;
+  }
+  const int64_t nrows = batch * seq * heads;
+  if (nrows == 0) return H3B_OK;
+  H3B_REQUIRE(aligned16(x) && aligned16(out) && aligned16(weight),
+              "qknorm_rope: x, out and weight must be 16-byte aligned");
+  const bool shuffle = rotary_dim % 16 == 0 && aligned16(cos) && aligned16(sin);
+  const int rot = (int)rotary_dim;
+  auto* o = (__nv_bfloat16*)out;
+  auto* xi = (const __nv_bfloat16*)x;
+  auto* w = (const __nv_bfloat16*)weight;
+#define H3B_QK(DD)                                                                         \
+  if (head_dim == DD) {                                                                    \
+    if (shuffle)                                                                           \
+      h3b::launch_qkrope<DD, true>(o, xi, w, cos, sin, nrows, heads, seq, rot, eps, stream); \
+    else                                                                                   \
+      h3b::launch_qkrope<DD, false>(o, xi, w, cos, sin, nrows, heads, seq, rot, eps, stream); \
+  }
+  H3B_QK(64) H3B_QK(128) H3B_QK(256)
+#undef H3B_QK
+  return h3b::check_launch("h3b_qknorm_rope");
+}
+
+extern "C" int h3b_qknorm_rope_pack(void* send, const void* q, const void* k, const void* v,
+                                    int64_t q_row_stride, int64_t k_row_stride,
+                                    int64_t v_row_stride, const void* q_weight,
+                                    const void* k_weight, const float* cos, const float* sin,
+                                    int64_t rows, int64_t heads, int64_t head_dim,
+                                    int64_t rotary_dim, int64_t world, float q_eps,
+                                    float k_eps, h3b_stream_t stream) {
+  H3B_REQUIRE(rows >= 0 && heads > 0 && world > 0, "qknorm_rope_pack: bad shape");
+  H3B_REQUIRE(heads % world == 0, "heads (%lld) must divide Ulysses degree (%lld)",
+              (long long)heads, (long long)world);
+  H3B_REQUIRE(rotary_dim >= 0 && rotary_dim <= head_dim && rotary_dim % 2 == 0,
+              "fused qknorm+rope requires an even rotary dimension no wider than the head, "
+              "got rotary_dim=%lld, head_dim=%lld",
+              (long long)rotary_dim, (long long)head_dim);
+  if (head_dim != 64 && head_dim != 128 && head_dim != 256) {
+    h3b::set_error("qknorm_rope_pack: head_dim must be 64, 128 or 256");
+    return H3B_ERR_UNSUPPORTED;
+  }
+  if (rows == 0) return H3B_OK;
+  H3B_REQUIRE(rows <= 0x7fffffffLL, "qknorm_rope_pack: too many rows");
+  H3B_REQUIRE(aligned16(send) && aligned16(q) && aligned16(k) && aligned16(v) &&
+                  aligned16(q_weight) && aligned16(k_weight) && q_row_stride % 8 == 0 &&
+                  k_row_stride % 8 == 0 && v_row_stride % 8 == 0,
+              "qknorm_rope_pack: tensors must be 16-byte aligned with row strides "
+              "divisible by 8");
+  const bool shuffle = rotary_dim % 16 == 0 && aligned16(cos) && aligned16(sin);
+  const int hl = (int)(heads / world);
+  auto* o = (__nv_bfloat16*)send;
+#define H3B_QKP(DD, SH)                                                                   \
+  h3b::qknorm_rope_pack_kernel<DD, SH><<<(unsigned)rows, 256, 0, stream>>>(                 \
+      o, (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,        \
+      q_row_stride, k_row_stride, v_row_stride, (const __nv_bfloat16*)q_weight,            \
+      (const __nv_bfloat16*)k_weight, cos, sin, rows, (int)heads, hl, (int)rotary_dim,     \
+      q_eps, k_eps)
+  if (head_dim == 64) {
+    if (shuffle) H3B_QKP(64, true); else H3B_QKP(64, false);
+  } else if (head_dim == 128) {
+    if (shuffle) H3B_QKP(128, true); else H3B_QKP(128, false);
+  } else {
+    if (shuffle) H3B_QKP(256, true); else H3B_QKP(256, false);
+  }
+#undef H3B_QKP
+  return h3b::check_launch("h3b_qknorm_rope_pack");
+}
+
+extern "C" int h3b_pack_qkv(void* out, const void* q, const void* k, const void* v,
+                            int64_t rows, int64_t heads, int64_t head_dim, int64_t world,
+                            int64_t q_row_stride, int64_t q_head_stride, int64_t k_row_stride,
+                            int64_t k_head_stride, int64_t v_row_stride,
+                            int64_t v_head_stride, h3b_stream_t stream) {
+  H3B_REQUIRE(rows >= 0 && heads >= 0 && head_dim >= 0 && world > 0, "pack_qkv: bad shape");
+  H3B_REQUIRE(heads % world == 0, "heads (%lld) must divide Ulysses degree (%lld)",
+              (long long)heads, (long long)world);
+  if (rows == 0 || heads == 0 || head_dim == 0) return H3B_OK;
+  const int64_t hl = heads / world;
+  auto* o = (__nv_bfloat16*)out;
+  auto* qq = (const __nv_bfloat16*)q;
+  auto* kk = (const __nv_bfloat16*)k;
+  auto* vv = (const __nv_bfloat16*)v;
+  const bool vec = (head_dim == 64 || head_dim == 128 || head_dim == 256) && rows <= 0x7fffffffLL &&
+                   aligned16(out) && aligned16(q) && aligned16(k) && aligned16(v) &&
+                   q_row_stride % 8 == 0 && q_head_stride % 8 == 0 && k_row_stride % 8 == 0 &&
+                   k_head_stride % 8 == 0 && v_row_stride % 8 == 0 && v_head_stride % 8 == 0;
+  if (vec) {
+#define H3B_PK(DD)                                                                       \
+  if (head_dim == DD)                                                                    \
+    h3b::pack_qkv_kernel<DD><<<(unsigned)rows, 256, 0, stream>>>(                          \
+        o, qq, kk, vv, rows, (int)heads, (int)hl, q_row_stride, q_head_stride, k_row_stride, \
+        k_head_stride, v_row_stride, v_head_stride);
+    H3B_PK(64) H3B_PK(128) H3B_PK(256)
+#undef H3B_PK
+  } else {
+    h3b::pack_qkv_scalar<<<(unsigned)(h3b::num_sms() * 8), 256, 0, stream>>>(
+        o, qq, kk, vv, rows, heads, hl, head_dim, q_row_stride, q_head_stride, k_row_stride,
+        k_head_stride, v_row_stride, v_head_stride);
+  }
+  return h3b::check_launch("h3b_pack_qkv");
+}
+
+extern "C" int h3b_merge_heads(void* out, const void* x, int64_t world, int64_t rows,
+                               int64_t inner, h3b_stream_t stream) {
+  H3B_REQUIRE(world >= 0 && rows >= 0 && inner >= 0, "merge_heads: negative shape");
+  if (world == 0 || rows == 0 || inner == 0) return H3B_OK;
+  auto* o = (__nv_bfloat16*)out;
+  auto* xi = (const __nv_bfloat16*)x;
+  if (inner % 8 == 0 && aligned16(out) && aligned16(x) && rows <= 0x7fffffffLL) {
+    h3b::merge_heads_vec<<<(unsigned)rows, 256, 0, stream>>>(o, xi, world, rows, inner / 8);
+  } else {
+    h3b::merge_heads_scalar<<<(unsigned)(h3b::num_sms() * 8), 256, 0, stream>>>(o, xi, world,
+                                                                               rows, inner);
+  }
+  return h3b::check_launch("h3b_merge_heads");
+}

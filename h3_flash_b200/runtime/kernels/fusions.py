@@ -1,0 +1,223 @@
+"""Fused transformer elementwise ops of the H3 block, backed by sm_100a CUDA kernels.
+
+Drop-in for ``h3_flash.runtime.kernels.fusions`` (src/h3_flash/runtime/kernels/fusions.py):
+the same function names, arguments, return shapes and ownership rules (outputs
+are fresh tensors, inputs are never mutated, non-contiguous activations are
+copied). The reference's Triton kernels become calls into libh3b.so; there is
+no CPU path, non-CUDA tensors raise.
+
+Additional ops the BASELINE block needs (no reference kernel): ``fused_modulate``,
+``fused_gated_residual``, ``fused_gelu_tanh`` and ``fused_qknorm_rope_pack``
+(QK-norm + RoPE fused with the packed-Ulysses destination-major pack).
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ... import _lib
+from ..._torch import (
+    call,
+    index64,
+    ptr,
+    require_bf16,
+    require_cuda,
+    rows_view,
+    stream_of,
+    table_rows,
+)
+
+
+def _available() -> bool:
+    try:
+        _lib.load()
+        return True
+    except Exception:
+        return False
+
+
+# The reference exposes HAVE_TRITON; this build's kernels live in libh3b.so.
+HAVE_CUDA_KERNELS = _available()
+
+
+def fused_rmsnorm_modulate(x, weight, scale, shift, index, eps):
+    """RMSNorm(x)*weight*(1+scale[idx])+shift[idx], idx = index[row % len(index)].
+    Reference: fusions.py:194-215."""
+
+    op = "fused_rmsnorm_modulate"
+    require_cuda(op, x, weight, scale, shift)
+    require_bf16(op, x, weight, scale, shift)
+    columns = x.shape[-1]
+    flat = rows_view(x)
+    scale, scale_stride = table_rows(scale)
+    shift, shift_stride = table_rows(shift)
+    idx = index64(index, x.device)
+    output = torch.empty(flat.shape, dtype=x.dtype, device=x.device)
+    call(
+        "h3b_rmsnorm_modulate", ptr(output), ptr(flat), ptr(weight.contiguous()), ptr(scale),
+        ptr(shift), ptr(idx), flat.shape[0], columns, idx.numel(), flat.stride(0),
+        output.stride(0), scale_stride, shift_stride, float(eps), stream_of(x),
+    )
+    return output.view(x.shape)
+
+
+def fused_residual_gate_rmsnorm_modulate(residual, branch, gate, weight, scale, shift, index, eps):
+    """hidden = residual + gate[idx]*branch; normed = RMSNorm(hidden)*weight*(1+scale)+shift.
+    Returns (hidden, normed). Reference: fusions.py:218-248."""
+
+    op = "fused_residual_gate_rmsnorm_modulate"
+    require_cuda(op, residual, branch, gate, weight, scale, shift)
+    require_bf16(op, residual, branch, gate, weight, scale, shift)
+    columns = residual.shape[-1]
+    residual_flat = residual.reshape(-1, columns).contiguous()
+    branch_flat = branch.reshape(-1, columns).contiguous()
+    if residual_flat.shape != branch_flat.shape:
+        raise ValueError("residual and branch must have the same shape")
+    gate, gate_stride = table_rows(gate)
+    scale, scale_stride = table_rows(scale)
+    shift, shift_stride = table_rows(shift)
+    idx = index64(index, residual.device)
+    hidden = torch.empty_like(residual_flat)
+    normed = torch.empty_like(residual_flat)
+    call(
+        "h3b_residual_gate_rmsnorm_modulate", ptr(hidden), ptr(normed), ptr(residual_flat),
+        ptr(branch_flat), ptr(weight.contiguous()), ptr(gate), ptr(scale), ptr(shift), ptr(idx),
+        residual_flat.shape[0], columns, idx.numel(), residual_flat.stride(0), gate_stride,
+        scale_stride, shift_stride, float(eps), stream_of(residual),
+    )
+    return hidden.view(residual.shape), normed.view(residual.shape)
+
+
+def fused_swiglu(x):
+    """out = x[..., :n] * silu(x[..., n:]), n = last/2 (value first, gate second).
+    Reference: fusions.py:251-265."""
+
+    op = "fused_swiglu"
+    require_cuda(op, x)
+    require_bf16(op, x)
+    if x.shape[-1] % 2:
+        raise ValueError("fused_swiglu needs an even last dimension")
+    columns = x.shape[-1] // 2
+    flat = rows_view(x)
+    output = torch.empty(flat.shape[0], columns, dtype=x.dtype, device=x.device)
+    call("h3b_swiglu", ptr(output), ptr(flat), flat.shape[0], columns, flat.stride(0),
+         output.stride(0), stream_of(x))
+    return output.view(*x.shape[:-1], columns)
+
+
+def fused_qknorm_rope(x, weight, cos, sin, eps):
+    """Per-head RMSNorm(x)*weight then rotate-half RoPE on the first rotary_dim columns.
+    x: [B, S, H, D]; cos/sin: [S, rotary_dim]. Reference: fusions.py:268-293."""
+
+    op = "fused_qknorm_rope"
+    batch, sequence, heads, head_dim = x.shape
+    rotary_dim = cos.shape[-1]
+    if rotary_dim > head_dim or rotary_dim % 2:
+        raise ValueError(
+            "fused qknorm+rope requires an even rotary dimension no wider "
+            f"than the head, got rotary_dim={rotary_dim}, head_dim={head_dim}"
+        )
+    require_cuda(op, x, weight, cos, sin)
+    require_bf16(op, x, weight)
+    flat = x.contiguous()
+    cos32 = cos.to(torch.float32).contiguous()
+    sin32 = sin.to(torch.float32).contiguous()
+    output = torch.empty_like(flat)
+    call("h3b_qknorm_rope", ptr(output), ptr(flat), ptr(weight.contiguous()), ptr(cos32),
+         ptr(sin32), batch, sequence, heads, head_dim, rotary_dim, float(eps), stream_of(x))
+    return output.view(batch, sequence, heads, head_dim)
+
+
+def fused_modulate(x, scale, shift, index=None):
+    """AdaLN modulate without the norm: x*(1+scale[idx])+shift[idx] (BASELINE op).
+    scale/shift are [d] vectors or [n_table, d] tables addressed through ``index``."""
+
+    op = "fused_modulate"
+    require_cuda(op, x, scale, shift)
+    require_bf16(op, x, scale, shift)
+    flat = rows_view(x)
+    scale, scale_stride = table_rows(scale)
+    shift, shift_stride = table_rows(shift)
+    idx = index64(index, x.device)
+    output = torch.empty(flat.shape, dtype=x.dtype, device=x.device)
+    call("h3b_modulate", ptr(output), ptr(flat), ptr(scale), ptr(shift), ptr(idx), flat.shape[0],
+         flat.shape[1], idx.numel(), flat.stride(0), output.stride(0), scale_stride,
+         shift_stride, stream_of(x))
+    return output.view(x.shape)
+
+
+def fused_gated_residual(residual, branch, gate, index=None):
+    """residual + gate[idx]*branch in one pass (the block's closing residual,
+    kernels/transformer.py:123-126)."""
+
+    op = "fused_gated_residual"
+    require_cuda(op, residual, branch, gate)
+    require_bf16(op, residual, branch, gate)
+    columns = residual.shape[-1]
+    residual_flat = residual.reshape(-1, columns).contiguous()
+    branch_flat = branch.reshape(-1, columns).contiguous()
+    if residual_flat.shape != branch_flat.shape:
+        raise ValueError("residual and branch must have the same shape")
+    gate, gate_stride = table_rows(gate)
+    idx = index64(index, residual.device)
+    output = torch.empty_like(residual_flat)
+    call("h3b_gated_residual", ptr(output), ptr(residual_flat), ptr(branch_flat), ptr(gate),
+         ptr(idx), residual_flat.shape[0], columns, idx.numel(), residual_flat.stride(0),
+         gate_stride, stream_of(residual))
+    return output.view(residual.shape)
+
+
+def fused_gelu_tanh(x):
+    """torch.nn.functional.gelu(x, approximate="tanh") in one bf16 pass."""
+
+    op = "fused_gelu_tanh"
+    require_cuda(op, x)
+    require_bf16(op, x)
+    flat = rows_view(x)
+    output = torch.empty(flat.shape, dtype=x.dtype, device=x.device)
+    call("h3b_gelu_tanh", ptr(output), ptr(flat), flat.shape[0], flat.shape[1], flat.stride(0),
+         output.stride(0), stream_of(x))
+    return output.view(x.shape)
+
+
+def fused_qknorm_rope_pack(q, k, v, q_weight, k_weight, cos, sin, world, q_eps, k_eps,
+                           out=None):
+    """QK-norm+RoPE of q and k fused with the packed-Ulysses destination-major pack.
+
+    q, k, v: [rows, heads, head_dim] with contiguous heads inside a row (row stride
+    free, e.g. views into one fused QKV projection). cos/sin: [rows, rotary_dim] or
+    None (norm only). Returns [world, rows, heads/world, 3*head_dim] equal to
+    ``pack_qkv_destination_major(fused_qknorm_rope(q), fused_qknorm_rope(k), v, world)``
+    (src/h3_flash/runtime/parallel/packed_ulysses.py:178-200)."""
+
+    op = "fused_qknorm_rope_pack"
+    rows, heads, head_dim = q.shape
+    if heads % world:
+        raise ValueError(f"heads ({heads}) must divide Ulysses degree ({world})")
+    if k.shape != q.shape or v.shape != q.shape:
+        raise ValueError("q, k and v must have the same shape")
+    require_cuda(op, q, k, v, q_weight, k_weight)
+    require_bf16(op, q, k, v, q_weight, k_weight)
+    for t in (q, k, v):
+        if t.stride(-1) != 1 or t.stride(-2) != head_dim:
+            raise ValueError(f"{op}: heads must be contiguous within a row")
+    if cos is None:
+        rotary_dim = 0
+        cos32 = sin32 = torch.empty(0, dtype=torch.float32, device=q.device)
+    else:
+        rotary_dim = cos.shape[-1]
+        if rotary_dim > head_dim or rotary_dim % 2:
+            raise ValueError(
+                "fused qknorm+rope requires an even rotary dimension no wider "
+                f"than the head, got rotary_dim={rotary_dim}, head_dim={head_dim}"
+            )
+        cos32 = cos.to(torch.float32).contiguous()
+        sin32 = sin.to(torch.float32).contiguous()
+    hl = heads // world
+    if out is None:
+        out = torch.empty((world, rows, hl, 3 * head_dim), dtype=q.dtype, device=q.device)
+    call("h3b_qknorm_rope_pack", ptr(out), ptr(q), ptr(k), ptr(v), q.stride(0), k.stride(0),
+         v.stride(0), ptr(q_weight.contiguous()), ptr(k_weight.contiguous()), ptr(cos32),
+         ptr(sin32), rows, heads, head_dim, rotary_dim, world, float(q_eps), float(k_eps),
+         stream_of(q))
+    return out

@@ -1,0 +1,166 @@
+/*
+ * h3b.h — C ABI of libh3b.so, the B200 (sm_100a) kernels behind the LOSSLESS
+ * packed-Ulysses DiT block of H3-Flash.
+ *
+ * Every entry point:
+ *   - takes raw device pointers, element counts and element strides (no
+ *     framework types), plus the CUDA stream to enqueue on;
+ *   - is stream-ordered: it never synchronises the host and never allocates;
+ *   - returns H3B_OK (0) or an error code; h3b_last_error() then returns a
+ *     message for the calling thread.
+ * Tensors are bf16 (IEEE bfloat16 bit patterns) unless stated; RoPE tables are
+ * fp32; AdaLN table indices are int64. Strides are in elements.
+ *
+ * Each declaration names the reference interface it replaces
+ * (fluxmatrix/h3-flash, paths relative to the project root).
+ */
+#ifndef H3B_H_
+#define H3B_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* h3b_stream_t; /* == cudaStream_t */
+
+#define H3B_OK 0
+#define H3B_ERR_VALUE 1       /* bad shape / argument: Python raises ValueError   */
+#define H3B_ERR_CUDA 2        /* CUDA launch or driver error: RuntimeError         */
+#define H3B_ERR_UNSUPPORTED 3 /* valid input this build does not handle: RuntimeError */
+
+#define H3B_ABI_VERSION 1
+
+int h3b_abi_version(void);
+/* Message of the last failing call on this host thread ("" if none). */
+const char* h3b_last_error(void);
+
+/* Device-side status word shared by all kernels of this library on the current
+ * device. Bounded waits inside kernels that time out OR a bit into it instead of
+ * spinning forever. h3b_device_status() copies it to the host (synchronous);
+ * h3b_clear_device_status() zeroes it (stream-ordered). Bits:
+ *   1 = attention pipeline wait timed out. */
+int h3b_device_status(int* status_out);
+int h3b_clear_device_status(h3b_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * AdaLN / norm elementwise ops. Rows are `rows` vectors of `cols` values.
+ * `index` holds `n_index` int64 table-row ids; row r reads table row
+ * index[r % n_index] of scale/shift/gate (each addressed with its own row
+ * stride). All math is fp32 with one rounding to bf16 at each store.
+ * ------------------------------------------------------------------------- */
+
+/* out = RMSNorm(x)*weight*(1+scale[idx])+shift[idx]
+ * replaces fused_rmsnorm_modulate  src/h3_flash/runtime/kernels/fusions.py:194
+ *          (_rmsnorm_modulate_kernel fusions.py:69-96) */
+int h3b_rmsnorm_modulate(void* out, const void* x, const void* weight,
+                         const void* scale, const void* shift, const int64_t* index,
+                         int64_t rows, int64_t cols, int64_t n_index,
+                         int64_t x_row_stride, int64_t out_row_stride,
+                         int64_t scale_row_stride, int64_t shift_row_stride,
+                         float eps, h3b_stream_t stream);
+
+/* hidden = residual + gate[idx]*branch (stored); normed = RMSNorm(hidden_fp32)*weight*(1+scale)+shift
+ * replaces fused_residual_gate_rmsnorm_modulate  fusions.py:218
+ *          (_residual_gate_rmsnorm_modulate_kernel fusions.py:23-67) */
+int h3b_residual_gate_rmsnorm_modulate(void* hidden_out, void* normed_out,
+                                       const void* residual, const void* branch,
+                                       const void* weight, const void* gate,
+                                       const void* scale, const void* shift,
+                                       const int64_t* index, int64_t rows, int64_t cols,
+                                       int64_t n_index, int64_t row_stride,
+                                       int64_t gate_row_stride, int64_t scale_row_stride,
+                                       int64_t shift_row_stride, float eps,
+                                       h3b_stream_t stream);
+
+/* out = x*(1+scale[idx])+shift[idx]   (AdaLN modulate without the norm)
+ * eager semantics of kernels/transformer.py:72-74 minus norm1; no reference kernel */
+int h3b_modulate(void* out, const void* x, const void* scale, const void* shift,
+                 const int64_t* index, int64_t rows, int64_t cols, int64_t n_index,
+                 int64_t x_row_stride, int64_t out_row_stride, int64_t scale_row_stride,
+                 int64_t shift_row_stride, h3b_stream_t stream);
+
+/* out = residual + gate[idx]*branch   (gated residual add)
+ * eager semantics of kernels/transformer.py:123-126 (block output); no reference kernel */
+int h3b_gated_residual(void* out, const void* residual, const void* branch,
+                       const void* gate, const int64_t* index, int64_t rows,
+                       int64_t cols, int64_t n_index, int64_t row_stride,
+                       int64_t gate_row_stride, h3b_stream_t stream);
+
+/* out[r, :n] = x[r, :n] * silu(x[r, n:2n])
+ * replaces fused_swiglu  fusions.py:251 (_swiglu_kernel fusions.py:98-123) */
+int h3b_swiglu(void* out, const void* x, int64_t rows, int64_t n,
+               int64_t in_row_stride, int64_t out_row_stride, h3b_stream_t stream);
+
+/* out = gelu(x, approximate="tanh") elementwise over rows x cols
+ * the FFN activation of the BASELINE block (torch.nn.functional.gelu semantics) */
+int h3b_gelu_tanh(void* out, const void* x, int64_t rows, int64_t cols,
+                  int64_t in_row_stride, int64_t out_row_stride, h3b_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Per-head QK RMSNorm + partial rotate-half RoPE, and the packed-Ulysses
+ * relayouts.
+ * ------------------------------------------------------------------------- */
+
+/* x, out: contiguous [batch, seq, heads, head_dim]; cos/sin fp32 [seq, rotary_dim]
+ * (row stride rotary_dim). out = rope(RMSNorm_D(x)*weight) on columns < rotary_dim,
+ * RMSNorm_D(x)*weight above.
+ * replaces fused_qknorm_rope  fusions.py:268 (_qknorm_partial_rope_kernel fusions.py:125-175) */
+int h3b_qknorm_rope(void* out, const void* x, const void* weight, const float* cos,
+                    const float* sin, int64_t batch, int64_t seq, int64_t heads,
+                    int64_t head_dim, int64_t rotary_dim, float eps,
+                    h3b_stream_t stream);
+
+/* Fused QK-norm+RoPE of q and k, plus the destination-major pack of q, k, v:
+ * send[dst, row, h, 0:D | D:2D | 2D:3D] = (rope(norm(q)), rope(norm(k)), v)[row, dst*hl+h]
+ * with hl = heads/world. q/k/v rows are strided (q_row_stride etc.; heads are
+ * contiguous within a row: head stride = head_dim). cos/sin fp32 [rows, rotary_dim].
+ * replaces fused_qknorm_rope (x2) + pack_qkv_destination_major
+ *          src/h3_flash/runtime/parallel/packed_ulysses.py:178-200, relayout.py:97-130 */
+int h3b_qknorm_rope_pack(void* send, const void* q, const void* k, const void* v,
+                         int64_t q_row_stride, int64_t k_row_stride, int64_t v_row_stride,
+                         const void* q_weight, const void* k_weight, const float* cos,
+                         const float* sin, int64_t rows, int64_t heads, int64_t head_dim,
+                         int64_t rotary_dim, int64_t world, float q_eps, float k_eps,
+                         h3b_stream_t stream);
+
+/* out[dst, row, h, :] = (q|k|v)[row, dst*hl + h, :], out is [world, rows, hl, 3*head_dim].
+ * q/k/v are [rows, heads, head_dim] with element strides (row, head), last dim contiguous.
+ * replaces pack_qkv_destination_major  src/h3_flash/runtime/parallel/relayout.py:97-130 */
+int h3b_pack_qkv(void* out, const void* q, const void* k, const void* v, int64_t rows,
+                 int64_t heads, int64_t head_dim, int64_t world,
+                 int64_t q_row_stride, int64_t q_head_stride,
+                 int64_t k_row_stride, int64_t k_head_stride,
+                 int64_t v_row_stride, int64_t v_head_stride, h3b_stream_t stream);
+
+/* out[row, src, :] = x[src, row, :] for contiguous x [world, rows, inner]
+ * replaces merge_heads  src/h3_flash/runtime/parallel/relayout.py:133-159 */
+int h3b_merge_heads(void* out, const void* x, int64_t world, int64_t rows,
+                    int64_t inner, h3b_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Dense non-causal attention, softmax(q k^T * scale) v, bf16 in/out, fp32
+ * accumulation; tcgen05 MMA with TMEM accumulators, TMA-fed.
+ * q/k/v/out are [batch, seq, heads, head_dim] views given by element strides
+ * (batch, row, head); head_dim must be 128 and contiguous; every stride must
+ * be a multiple of 8 elements and every base 16-byte aligned.
+ * The packed-Ulysses receive buffer [S, hl, 3D] is the view
+ *   q = qkv, k = qkv + D, v = qkv + 2D, row stride hl*3D, head stride 3D.
+ * replaces torch SDPA at src/h3_flash/runtime/parallel/packed_ulysses.py:201-209 and
+ *          flash_attn_func in src/h3_flash/runtime/attention/dense_fa4.py:74-81, :145
+ * ------------------------------------------------------------------------- */
+int h3b_attention(void* out, const void* q, const void* k, const void* v,
+                  int64_t batch, int64_t seq_q, int64_t seq_k, int64_t heads,
+                  int64_t head_dim,
+                  int64_t q_batch_stride, int64_t q_row_stride, int64_t q_head_stride,
+                  int64_t k_batch_stride, int64_t k_row_stride, int64_t k_head_stride,
+                  int64_t v_batch_stride, int64_t v_row_stride, int64_t v_head_stride,
+                  int64_t o_batch_stride, int64_t o_row_stride, int64_t o_head_stride,
+                  float softmax_scale, h3b_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* H3B_H_ */

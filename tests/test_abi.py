@@ -1,0 +1,67 @@
+"""The C-ABI library loads without a GPU and exports exactly what include/h3b.h declares.
+
+Only argument-validation paths are called here (they return before touching CUDA).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from h3_flash_b200 import _lib
+
+HEADER = Path(__file__).resolve().parents[1] / "include" / "h3b.h"
+
+
+def declared_functions() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(h3b_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_hot_path():
+    names = declared_functions()
+    for expected in (
+        "h3b_rmsnorm_modulate", "h3b_residual_gate_rmsnorm_modulate", "h3b_modulate", "h3b_gated_residual",
+        "h3b_swiglu", "h3b_gelu_tanh", "h3b_qknorm_rope", "h3b_qknorm_rope_pack", "h3b_pack_qkv",
+        "h3b_merge_heads", "h3b_attention", "h3b_last_error", "h3b_abi_version",
+    ):
+        assert expected in names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    assert set(declared_functions()) <= set(_lib.exported_symbols())
+
+
+def test_abi_version():
+    assert _lib.load().h3b_abi_version() == _lib.ABI_VERSION
+
+
+def test_shape_errors_map_to_value_error_without_a_gpu():
+    lib = _lib.load()
+    code = lib.h3b_rmsnorm_modulate(None, None, None, None, None, None, -1, 8, 1, 8, 8, 8, 8,
+                                    ctypes.c_float(1e-6), None)
+    assert code == _lib.H3B_ERR_VALUE
+    assert "negative shape" in lib.h3b_last_error().decode()
+    with pytest.raises(ValueError, match="must divide Ulysses degree"):
+        _lib.call("h3b_pack_qkv", None, None, None, None, 4, 6, 128, 4, 0, 0, 0, 0, 0, 0, None)
+    with pytest.raises(ValueError, match="rotary dimension"):
+        _lib.call("h3b_qknorm_rope", None, None, None, None, None, 1, 4, 2, 128, 7, 1e-6, None)
+
+
+def test_unsupported_head_dim_is_a_runtime_error():
+    with pytest.raises(RuntimeError, match="head_dim must be 128"):
+        _lib.call("h3b_attention", None, None, None, None, *([1] * 4), 64, *([64] * 12), 1.0, None)
+
+
+def test_empty_inputs_are_noops():
+    # rows == 0 returns before any launch
+    _lib.call("h3b_swiglu", None, None, 0, 16, 32, 16, None)
+    _lib.call("h3b_merge_heads", None, None, 2, 0, 128, None)
+    _lib.call("h3b_attention", None, None, None, None, 1, 0, 5, 1, 128, *([128] * 12), 1.0, None)

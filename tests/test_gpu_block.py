@@ -1,0 +1,73 @@
+"""Whole-block parity on one GPU: the installed fused block vs the fp32 CPU oracle.
+
+Bar (north star): max-abs <= 2e-2 and cosine >= 0.9999 against the fp32 reference.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle.attention_ref import error_metrics
+from oracle.block_ref import block_forward, fp32_params
+
+pytestmark = pytest.mark.gpu
+
+MAX_ABS = 2e-2
+COSINE = 0.9999
+
+
+def _setup(rows: int, dim: int, heads: int, ffn: int, activation: str, seed: int = 0):
+    from h3_flash_b200.runtime.h3_block import H3BlockStack, H3TransformerBlock
+    from h3_flash_b200.workloads import init_block_, rope_tables
+
+    block = init_block_(H3TransformerBlock(dim=dim, heads=heads, head_dim=128, ffn_inner=ffn,
+                                           activation=activation), seed=seed)
+    block = block.to(device="cuda", dtype=torch.bfloat16)
+    stack = H3BlockStack([block])
+    g = torch.Generator().manual_seed(seed + 1)
+    hidden = torch.randn(1, rows, dim, generator=g).to(torch.bfloat16)
+    idx = torch.randint(0, 3, (rows,), generator=g)
+    pos = torch.stack([torch.arange(rows) // 64, (torch.arange(rows) // 8) % 8, torch.arange(rows) % 8], -1)
+    cos, sin = rope_tables(pos, 96)
+    return stack, block, hidden, idx, cos, sin
+
+
+@pytest.mark.parametrize("rows,dim,heads,ffn,activation", [(300, 384, 3, 1536, "gelu-tanh"),
+                                                           (257, 256, 2, 1024, "swiglu"),
+                                                           (1024, 3072, 24, 12288, "gelu-tanh")])
+def test_fused_block_matches_oracle(rows, dim, heads, ffn, activation):
+    from h3_flash_b200.runtime.kernels import install_transformer_fusions
+
+    stack, block, hidden, idx, cos, sin = _setup(rows, dim, heads, ffn, activation)
+    params = fp32_params(block)
+    ref = block_forward(params, hidden[0].float(), idx, cos, sin, heads=heads, head_dim=128, eps=1e-6,
+                        qk_eps=1e-6, activation=activation)
+    runtime = install_transformer_fusions(stack)
+    with torch.no_grad():
+        out = stack(hidden.cuda(), None, idx.cuda(), (cos.cuda(), sin.cuda()))
+    m = error_metrics(out[0].float().cpu().numpy(), ref.numpy())
+    assert m["max_abs"] <= MAX_ABS, m
+    assert m["cosine"] >= COSINE, m
+    # the reference's first-block gates were recorded
+    assert {"rmsnorm_modulate", "residual_chain", "residual_output"} <= set(runtime["gate"])
+    for name, gate in runtime["gate"].items():
+        assert gate["cosine"] > 0.999, (name, gate)
+
+
+def test_block_is_deterministic_and_reuses_qkv_cache():
+    from h3_flash_b200.runtime.kernels import install_transformer_fusions
+
+    stack, block, hidden, idx, cos, sin = _setup(256, 256, 2, 1024, "gelu-tanh")
+    install_transformer_fusions(stack)
+    args = (hidden.cuda(), None, idx.cuda(), (cos.cuda(), sin.cuda()))
+    with torch.no_grad():
+        a = stack(*args)
+        b = stack(*args)
+    assert torch.equal(a, b)
+    # in-place weight update invalidates the fused QKV weight cache
+    with torch.no_grad():
+        block.attn.to_q.weight.mul_(0.5)
+        c = stack(*args)
+    assert not torch.equal(a, c)

@@ -1,0 +1,131 @@
+"""Packed-Ulysses SP over NCCL on 2+ GPUs (skipped on single-GPU boxes).
+
+Each rank runs its contiguous row shard of the block through install_packed_ulysses;
+the result must match the single-GPU fused block within the block tolerance, and the
+packed exchange must equal the reference's separate per-tensor exchange bit for bit
+(check_packed_ulysses.py:20-62).
+"""
+
+from __future__ import annotations
+
+import datetime
+import os
+import socket
+import traceback
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, queue):
+    try:
+        os.environ["NCCL_NVLS_ENABLE"] = "0"
+        torch.cuda.set_device(rank)
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                                timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
+        from h3_flash_b200.runtime.h3_block import H3BlockStack, H3TransformerBlock
+        from h3_flash_b200.runtime.kernels import install_transformer_fusions
+        from h3_flash_b200.runtime.parallel import install_packed_ulysses
+        from h3_flash_b200.runtime.parallel.packed_ulysses import (
+            PackedUlyssesRuntime,
+            _packed_output_all_to_all,
+            _packed_qkv_all_to_all,
+        )
+        from h3_flash_b200.workloads import init_block_, rope_tables, split_bounds
+
+        # 1) exchange equality gate with deliberately uneven rows (check_packed_ulysses.py:65-127)
+        rows = 19 + (world - rank)
+        g = torch.Generator(device="cuda").manual_seed(1000 + rank)
+        q, k, v = (torch.randn(rows, 8 * world, 128, device="cuda", generator=g).to(torch.bfloat16) for _ in range(3))
+        runtime = PackedUlyssesRuntime(dist.group.WORLD)
+        runtime.begin_request()
+        packed = _packed_qkv_all_to_all(q, k, v, runtime)
+        counts = runtime.row_counts(rows)
+        refs = []
+        for t in (q, k, v):
+            send = t.reshape(rows, world, 8, 128).permute(1, 0, 2, 3).contiguous()
+            out = torch.empty(sum(counts) * 8 * 128, dtype=t.dtype, device="cuda")
+            dist.all_to_all_single(out, send.reshape(-1), output_split_sizes=[c * 8 * 128 for c in counts],
+                                   input_split_sizes=[rows * 8 * 128] * world)
+            refs.append(out.view(sum(counts), 8, 128))
+        qkv_equal = all(torch.equal(packed[..., i * 128 : (i + 1) * 128], refs[i]) for i in range(3))
+        attn = packed[..., :128].contiguous()
+        back = _packed_output_all_to_all(attn, rows, runtime)
+        back_equal = torch.equal(back, q)  # q went out and came back through both exchanges
+
+        # 2) full block: SP=world vs the same block on one GPU
+        heads, total = 2 * world, 1000
+        dim = 128 * heads
+        block = init_block_(H3TransformerBlock(dim=dim, heads=heads, head_dim=128, ffn_inner=4 * dim), seed=5)
+        block = block.to("cuda", torch.bfloat16)
+        ref_stack = H3BlockStack([block])
+        install_transformer_fusions(ref_stack)
+        gh = torch.Generator().manual_seed(9)
+        hidden = torch.randn(1, total, dim, generator=gh).to(torch.bfloat16).cuda()
+        idx = torch.randint(0, 3, (total,), generator=gh).cuda()
+        pos = torch.stack([torch.arange(total) // 100, (torch.arange(total) // 10) % 10, torch.arange(total) % 10], -1)
+        cos, sin = (t.cuda() for t in rope_tables(pos, 96))
+        with torch.no_grad():
+            full = ref_stack(hidden, None, idx, (cos, sin))
+        sp_block = init_block_(H3TransformerBlock(dim=dim, heads=heads, head_dim=128, ffn_inner=4 * dim), seed=5)
+        sp_stack = H3BlockStack([sp_block.to("cuda", torch.bfloat16)])
+        install_transformer_fusions(sp_stack)
+        sp_runtime = install_packed_ulysses(sp_stack)
+        sp_runtime.begin_request()
+        start, stop = split_bounds(total, world, rank)
+        with torch.no_grad():
+            local = sp_stack(hidden[:, start:stop].contiguous(), None, idx[start:stop], (cos[start:stop], sin[start:stop]))
+        diff = (local.float() - full[:, start:stop].float()).abs()
+        max_diff = float(diff.max())
+        cosine = float(torch.nn.functional.cosine_similarity(local.float().flatten(),
+                                                             full[:, start:stop].float().flatten(), dim=0))
+        # GEMMs over r vs S rows may pick different cuBLAS tilings, so the bar is the
+        # block tolerance, not bit equality.
+        block_equal = max_diff <= 2e-2 and cosine >= 0.9999
+        flags = torch.tensor([qkv_equal, back_equal, block_equal], dtype=torch.int32, device="cuda")
+        dist.all_reduce(flags, op=dist.ReduceOp.MIN)
+        queue.put((rank, True, (flags.tolist(), counts, max_diff, sp_runtime.attention_calls)))
+        dist.barrier()
+        dist.destroy_process_group()
+    except BaseException:  # noqa: BLE001
+        queue.put((rank, False, traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_packed_ulysses_sp_matches_single_gpu():
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 8)
+    ctx = mp.get_context("spawn")
+    queue = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, queue)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    try:
+        for _ in procs:
+            rank, ok, payload = queue.get(timeout=300)
+            assert ok, payload
+            results[rank] = payload
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.kill()
+    flags, counts, max_diff, calls = results[0]
+    assert counts == [19 + world - r for r in range(world)]
+    assert flags[0] == 1, "packed QKV exchange differs from per-tensor exchange"
+    assert flags[1] == 1, "output exchange + merge is not the inverse"
+    assert flags[2] == 1, f"SP block differs from single-GPU block (max diff {max_diff})"
+    assert calls == 1
