@@ -8,7 +8,7 @@ A step is one block forward over the whole joint sequence (S = 49,920 video + 1,
 audio tokens, d=3072, 24x128 heads, FFN 12,288 GELU-tanh, bf16), split into W
 contiguous row shards (Ulysses SP=W; strong scaling: total work fixed). Inputs are
 resident in HBM; each step is timed alone with CUDA events on the compute stream and
-L2 is flushed (256 MiB write) between steps. ms_per_step is the max over ranks.
+L2 is flushed (256 MiB written, then read back) between steps. ms_per_step is the max over ranks.
 
 ``e2e`` repeats the step through the same public API with the hidden states copied
 from pinned host memory before and the block output copied back after, inside the
@@ -307,7 +307,7 @@ def run_h3b(args) -> dict | None:
     _barrier(world)
     torch.cuda.synchronize()
     for _ in range(args.steps):
-        flush.fill_(1)
+        flush_l2(flush)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record(stream)
         step(hidden)
@@ -324,7 +324,7 @@ def run_h3b(args) -> dict | None:
     _barrier(world)
     torch.cuda.synchronize()
     for _ in range(args.steps):
-        flush.fill_(1)
+        flush_l2(flush)
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         s.record(stream)
         x = hidden_host.to("cuda", non_blocking=True)
@@ -360,7 +360,7 @@ def run_h3b(args) -> dict | None:
                 + 2 * r * cfg.ffn_inner * 2  # GELU: read, write
                 + 3 * r * d * 2          # gated residual: 2 reads, 1 write
                 + 2 * 3 * r * d * 2)     # qknorm+rope+pack: read qkv, write packed
-    ew_ms = sum(statistics.mean(v) for k, v in sections.items() if k in ("elementwise", "qknorm_rope_pack"))
+    ew_ms = sum(sum(v) / args.steps for k, v in sections.items() if k in ("elementwise", "qknorm_rope_pack"))
     ew_ms = _max_over_ranks(ew_ms, world)
     a2a_bytes = (4 * r * d * 2) * (world - 1) / world if world > 1 else 0.0
     a2a_ms = _max_over_ranks(sum(sections.get("all_to_all", [0.0])) / max(args.steps, 1), world)
@@ -386,7 +386,7 @@ def run_h3b(args) -> dict | None:
             "seq": cfg.seq, "video_tokens": cfg.video_tokens, "audio_tokens": cfg.audio_tokens,
             "dim": cfg.dim, "heads": cfg.heads, "head_dim": cfg.head_dim, "ffn": f"{cfg.ffn_inner} gelu-tanh",
             "rotary_dim": cfg.rotary_dim, "rows_per_rank": rows, "heads_per_rank": hl,
-            "parallelism": f"ulysses_sp{world}", "l2": "flushed (256 MiB write) between timed steps",
+            "parallelism": f"ulysses_sp{world}", "l2": "flushed between timed steps (256 MiB write, then read back)",
         },
         "e2e": {"value": round(e2e_mean, 4), "unit": "ms",
                 "h2d_bytes_per_step": hidden_host.numel() * hidden_host.element_size(),
@@ -423,6 +423,109 @@ def run_h3b(args) -> dict | None:
     return result
 
 
+def flush_l2(buf: torch.Tensor) -> None:
+    """Evict L2 between timed steps: write a buffer larger than L2, then read it back so
+    the dirty lines are written to DRAM here rather than inside the next timed step."""
+
+    buf.fill_(1)
+    buf.view(torch.int64).sum()
+
+
+def _timed(fn, steps: int, warmup: int, flush: torch.Tensor) -> float:
+    """Mean device ms of fn() over ``steps`` launches, L2 flushed before each."""
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    events = []
+    for _ in range(steps):
+        flush_l2(flush)
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        events.append((s, e))
+    torch.cuda.synchronize()
+    return statistics.mean(s.elapsed_time(e) for s, e in events)
+
+
+def elementwise_sweep(args) -> dict:
+    """BASELINE config 2: each fused elementwise kernel at the 1xB200 sweep shapes;
+    achieved GB/s = algorithmic bytes (each input read once, each output written once)
+    / CUDA-event time, L2 flushed between launches."""
+
+    from h3_flash_b200.runtime.kernels import fusions as F
+    from h3_flash_b200.workloads import CONFIGS, positions, rope_tables
+
+    torch.cuda.set_device(0)
+    cfg = CONFIGS["480p-5s"]
+    s, d = cfg.video_tokens, cfg.dim  # [1, 49920, 3072]
+    g = torch.Generator(device="cuda").manual_seed(0)
+    rnd = lambda *shape, std=1.0, mean=0.0: (torch.randn(*shape, device="cuda", generator=g) * std + mean).to(  # noqa: E731
+        torch.bfloat16)
+    x, br = rnd(1, s, d), rnd(1, s, d)
+    scale_v, shift_v, gate_v = rnd(d, std=0.1), rnd(d, std=0.1), rnd(d, std=0.1)  # BASELINE [d] vectors
+    table = rnd(3, 6 * d, std=0.1)
+    t = table.chunk(6, -1)
+    idx = torch.ones(s, dtype=torch.long, device="cuda")
+    w = rnd(d, std=0.02, mean=1.0)
+    qk = rnd(1, s, cfg.heads, cfg.head_dim)
+    qkw = rnd(cfg.head_dim, std=0.02, mean=1.0)
+    cos, sin = (z[:s].cuda() for z in rope_tables(positions(cfg), 96))
+    hidden = rnd(s, cfg.ffn_inner)
+    qkv = rnd(s, 3 * d)
+    q3, k3, v3 = (z.view(s, cfg.heads, cfg.head_dim) for z in qkv.split(d, -1))
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
+    e = s * d * 2  # bytes of one [1, S, d] bf16 tensor
+    peaks = _peaks()
+    cases = {
+        "modulate": (lambda: F.fused_modulate(x, scale_v, shift_v), 2 * e),
+        "gated_residual": (lambda: F.fused_gated_residual(x, br, gate_v), 3 * e),
+        "rmsnorm_modulate": (lambda: F.fused_rmsnorm_modulate(x, w, t[1], t[0], idx, 1e-6), 2 * e),
+        "residual_gate_rmsnorm_modulate": (
+            lambda: F.fused_residual_gate_rmsnorm_modulate(x, br, t[2], w, t[4], t[3], idx, 1e-6), 4 * e),
+        "qknorm_rope_rot96": (lambda: F.fused_qknorm_rope(qk, qkw, cos, sin, 1e-6), 2 * e + 2 * s * 96 * 4),
+        "qknorm_rope_pack_w8": (lambda: F.fused_qknorm_rope_pack(q3, k3, v3, qkw, qkw, cos, sin, 8, 1e-6, 1e-6),
+                                6 * e + 2 * s * 96 * 4),
+        "gelu_tanh_ffn": (lambda: F.fused_gelu_tanh(hidden), 2 * s * cfg.ffn_inner * 2),
+    }
+    out = {}
+    for name, (fn, nbytes) in cases.items():
+        ms = _timed(fn, args.steps, args.warmup, flush)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"ms": round(ms, 4), "bytes": nbytes, "gbs": round(gbs, 1),
+                     "frac_of_measured_hbm": round(gbs / peaks["hbm_gbs"], 4),
+                     "frac_of_8tbs_nominal": round(gbs / 8000.0, 4)}
+    return {"sweep": "elementwise", "shape": f"[1,{s},{d}] / [1,{s},24,128] / FFN [{s},{cfg.ffn_inner}]",
+            "hbm_peak_gbs": peaks["hbm_gbs"], "kernels": out}
+
+
+def profile_kernel(args) -> None:
+    """Launch one kernel family a few times for an ncu capture (no JSON contract)."""
+
+    from h3_flash_b200.runtime.attention.dense import packed_attention
+
+    torch.cuda.set_device(0)
+    from h3_flash_b200.workloads import CONFIGS
+
+    cfg = CONFIGS[args.config]
+    if args.profile_kernel == "attention":
+        g = torch.Generator(device="cuda").manual_seed(0)
+        packed = torch.randn(cfg.seq, args.heads_per_rank, 3 * cfg.head_dim, device="cuda",
+                             generator=g).to(torch.bfloat16)
+        for _ in range(args.warmup + args.steps):
+            packed_attention(packed, cfg.head_dim)
+    elif args.profile_kernel == "elementwise":
+        args.steps, args.warmup = max(args.steps, 1), max(args.warmup, 0)
+        elementwise_sweep(args)
+    torch.cuda.synchronize()
+    from h3_flash_b200 import _lib
+
+    if _lib.device_status():
+        raise RuntimeError("h3b device status set")
+    print(f"profile-kernel {args.profile_kernel} done")
+
+
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[1])
     parser.add_argument("--gpus", type=int, default=1)
@@ -431,9 +534,20 @@ def main() -> int:
     parser.add_argument("--impl", choices=["h3b", "reference"], default="h3b")
     parser.add_argument("--config", default="480p-5s")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--sweep", choices=["elementwise"], help="print the config-2 kernel sweep instead")
+    parser.add_argument("--profile-kernel", choices=["attention", "elementwise"],
+                        help="launch one kernel family for an ncu capture")
+    parser.add_argument("--heads-per-rank", type=int, default=3)
     args = parser.parse_args()
     sys.path.insert(0, str(ROOT))
     from h3_flash_b200.workloads import CONFIGS
+
+    if args.profile_kernel:
+        profile_kernel(args)
+        return 0
+    if args.sweep == "elementwise":
+        print(json.dumps(elementwise_sweep(args)), flush=True)
+        return 0
 
     if args.impl == "reference":
         rank = int(os.environ.get("RANK", "0"))

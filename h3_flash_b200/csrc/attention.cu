@@ -4,21 +4,28 @@
 // One CTA owns two 128-row query tiles of one (batch, head) and streams the
 // whole key/value sequence in 128-row blocks:
 //
-//   warp 8      TMA producer: Q0, Q1 once, then K_j / V_j into separate rings
-//               (3 K stages, 2 V stages, 32 KB each, 128B-swizzled).
-//   warp 9      MMA issuer (one thread): S_t = Q_t K_j^T into TMEM, then
+//   warp 16     TMA producer: Q0, Q1 once, then K_j / V_j into separate rings
+//               (2 K stages, 2 V stages, 32 KB each, 128B-swizzled).
+//   warp 17     MMA issuer (one thread): S_t = Q_t K_j^T into TMEM, then
 //               O_t += P_t V_j with P_t read from TMEM (A operand) and V_j from
-//               shared memory (MN-major B operand). Tiles t=0,1 alternate so the
-//               tensor core works on one tile while the other tile's softmax runs.
-//   warps 0-3   softmax of tile 0, warps 4-7 softmax of tile 1: thread i owns
-//               query row i (TMEM lane i). Reads S with tcgen05.ld, keeps the
-//               running max in the log2 domain, writes P (bf16) over S's first 64
-//               TMEM columns, accumulates the row sum in fp32. O is rescaled in
+//               shared memory (MN-major B operand), in two 64-key halves. Tiles
+//               t=0,1 alternate so the tensor core works on one tile while the
+//               other tile's softmax runs.
+//   warps 0-7   softmax of tile 0, warps 8-15 softmax of tile 1. Warp w owns
+//               TMEM lane quadrant w%4 (query rows 32(w%4)..+31) and key half
+//               (w/4)%2 of every block: two warps share each row, so each SMSP
+//               runs two softmax warps per tile and hides the TMEM/MUFU
+//               latencies of one with the other. Per block a warp streams its 64
+//               S columns from TMEM twice (pass 1: row max, exchanged with the
+//               partner warp through shared memory; pass 2: p = 2^(s*c - m)),
+//               writes P (bf16) over the S columns it has consumed and
+//               accumulates its share of the row sum in fp32. O is rescaled in
 //               TMEM only when the running max grows by more than 2^8 (P stays
 //               <= 256, exact in the fp32 accumulator), which after the first
 //               blocks is rare.
 //
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
+// P of key half h of tile t lives in S_t columns [64h, 64h+32).
 // A tcgen05.commit tracks every earlier MMA of the issuing thread, so the
 // commit after S_t(j) also certifies that PV_t(j-1) is done: the softmax may
 // touch O_t once it has seen S_t(j).
@@ -46,11 +53,12 @@ constexpr int kBlockM = 128;  // query rows per tile
 constexpr int kBlockN = 128;  // key rows per block
 constexpr int kHeadDim = 128;
 constexpr int kTiles = 2;  // query tiles per CTA
-constexpr int kKStages = 3;
+constexpr int kKStages = 2;
 constexpr int kVStages = 2;
-constexpr int kThreads = 320;  // 8 softmax warps + TMA warp + MMA warp
-constexpr int kLoadWarp = 8;
-constexpr int kMmaWarp = 9;
+constexpr int kSoftmaxWarps = 16;  // 8 per query tile: 4 TMEM lane quadrants x 2 key halves
+constexpr int kThreads = (kSoftmaxWarps + 2) * 32;  // + TMA warp + MMA warp
+constexpr int kLoadWarp = kSoftmaxWarps;
+constexpr int kMmaWarp = kSoftmaxWarps + 1;
 
 constexpr uint32_t kTileBytes = kBlockM * kHeadDim * 2;  // 32 KB: two 16 KB swizzled halves
 constexpr uint32_t kHalfBytes = kTileBytes / 2;
@@ -58,9 +66,12 @@ constexpr uint32_t kSmemQ = 0;
 constexpr uint32_t kSmemK = kSmemQ + kTiles * kTileBytes;
 constexpr uint32_t kSmemV = kSmemK + kKStages * kTileBytes;
 constexpr uint32_t kSmemBar = kSmemV + kVStages * kTileBytes;
-// barriers: q[2], kfull[3], kempty[3], vfull[2], vempty[2], s[2], p[2], o[2] + tmem slot + abort
-constexpr uint32_t kNumBars = kTiles + 2 * kKStages + 2 * kVStages + 3 * kTiles;
-constexpr uint32_t kSmemBytes = kSmemBar + kNumBars * 8 + 16;
+// barriers: q[2], kfull[3], kempty[3], vfull[2], vempty[2], s[2], p[2][2], o[2] + tmem slot + abort
+constexpr uint32_t kNumBars = kTiles + 2 * kKStages + 2 * kVStages + 4 * kTiles;
+// Row-max / row-sum exchange between the two warps that share a TMEM lane
+// quadrant: float [tile][parity][key half][128 rows].
+constexpr uint32_t kSmemXch = kSmemBar + ((kNumBars * 8 + 16 + 127) / 128) * 128;
+constexpr uint32_t kSmemBytes = kSmemXch + kTiles * 2 * 2 * kBlockM * 4;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;  // slack to 1024-align the base
 
 constexpr uint32_t kTmemCols = 512;
@@ -71,6 +82,15 @@ constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 
 // Rescale O only when the running row max (log2 units) grew by more than this.
 constexpr float kRescaleThreshold = 8.0f;
+
+// Of every 8 column pairs of S, this many take the FMA-pipe exp2 (exp2_poly)
+// instead of MUFU ex2: the softmax of one 128x128 block needs as many MUFU
+// cycles as the tensor core needs for that tile's two MMAs, so part of the
+// exponentials must move to the (otherwise idle) FMA pipe.
+#ifndef H3B_ATTN_POLY_PAIRS
+#define H3B_ATTN_POLY_PAIRS 2
+#endif
+constexpr int kPolyPairs = H3B_ATTN_POLY_PAIRS;
 
 // ---------------------------------------------------------------------------
 // PTX wrappers
@@ -263,6 +283,38 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+// 32 lanes x 16 columns -> 16 registers per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]),
+        "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld_wait16(uint32_t (&r)[16]) {
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]));
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7])
+      : "memory");
+}
+
+// bar.sync on a named barrier shared by `count` threads (a multiple of 32).
+__device__ __forceinline__ void named_bar_sync(uint32_t id, uint32_t count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
 __device__ __forceinline__ void tmem_st_wait() {
   asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
 }
@@ -271,6 +323,50 @@ __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Keys at block columns >= valid do not exist (sequence tail): score -inf.
+__device__ __forceinline__ void mask_keys(uint32_t (&r)[32], int col0, int valid) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i)
+    if (col0 + i >= valid) r[i] = __float_as_uint(-INFINITY);
+}
+
+__device__ __forceinline__ void mask_keys16(uint32_t (&r)[16], int col0, int valid) {
+#pragma unroll
+  for (int i = 0; i < 16; ++i)
+    if (col0 + i >= valid) r[i] = __float_as_uint(-INFINITY);
+}
+
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// 2^x for a pair of fp32 values on the FMA pipe (no MUFU):
+//   n = round(x) via the 1.5*2^23 shifter, f = x - n in [-1/2, 1/2],
+//   2^f ~ c0 + f(c1 + f(c2 + f c3)), then n is added to the exponent field.
+// The cubic is this file's own relative-error minimax fit of 2^f on [-1/2, 1/2]
+// (Lawson-weighted least squares over Chebyshev points): max relative error
+// 7.5e-5, below half a bf16 ulp (2^-9) of the P operand it feeds. Inputs are
+// clamped to >= -126 so the exponent add never wraps (masked -inf keys become
+// ~1e-38 instead of 0; their V rows are zero).
+__device__ __forceinline__ float2 exp2_poly(float2 x) {
+  x.x = fmaxf(x.x, -126.f);
+  x.y = fmaxf(x.y, -126.f);
+  const float kShift = 12582912.f;  // 1.5 * 2^23
+  const float2 t = __fadd2_rn(x, make_float2(kShift, kShift));
+  const float2 n = __fadd2_rn(t, make_float2(-kShift, -kShift));
+  const float2 f = __ffma2_rn(n, make_float2(-1.f, -1.f), x);
+  float2 p = __ffma2_rn(f, make_float2(0.0551716685f, 0.0551716685f),
+                        make_float2(0.2426111400f, 0.2426111400f));
+  p = __ffma2_rn(p, f, make_float2(0.6932609677f, 0.6932609677f));
+  p = __ffma2_rn(p, f, make_float2(0.9999280572f, 0.9999280572f));
+  float2 r;
+  r.x = __int_as_float(__float_as_int(p.x) + (__float_as_int(t.x) << 23));
+  r.y = __int_as_float(__float_as_int(p.y) + (__float_as_int(t.y) << 23));
+  return r;
 }
 
 // ---------------------------------------------------------------------------
@@ -303,11 +399,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto bar_vfull = [&](int s) { return bars + 8u * (kTiles + 2 * kKStages + s); };
   auto bar_vempty = [&](int s) { return bars + 8u * (kTiles + 2 * kKStages + kVStages + s); };
   auto bar_s = [&](int t) { return bars + 8u * (kTiles + 2 * kKStages + 2 * kVStages + t); };
-  auto bar_p = [&](int t) {
-    return bars + 8u * (kTiles + 2 * kKStages + 2 * kVStages + kTiles + t);
+  // bar_p(t, h): softmax of tile t has written P for keys [64h, 64h+64) of the block.
+  auto bar_p = [&](int t, int h) {
+    return bars + 8u * (kTiles + 2 * kKStages + 2 * kVStages + kTiles + 2 * t + h);
   };
   auto bar_o = [&](int t) {
-    return bars + 8u * (kTiles + 2 * kKStages + 2 * kVStages + 2 * kTiles + t);
+    return bars + 8u * (kTiles + 2 * kKStages + 2 * kVStages + 3 * kTiles + t);
   };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemBar + kNumBars * 8);
   volatile uint32_t* abort_flag = tmem_slot + 1;
@@ -323,7 +420,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < kTiles; ++t) {
       mbar_init(bar_q(t), 1);
       mbar_init(bar_s(t), 1);
-      mbar_init(bar_p(t), 128);
+      mbar_init(bar_p(t, 0), 128);
+      mbar_init(bar_p(t, 1), 128);
       mbar_init(bar_o(t), 1);
     }
     for (int s = 0; s < kKStages; ++s) {
@@ -388,24 +486,36 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc_pv = instr_desc(true);
       bool ok = true;
       for (int t = 0; t < kTiles && ok; ++t) ok = wait_bar(bar_q(t), 0, abort_flag, prm.status);
+      // Descriptors are built once: the issue loop only adds compile-time K-step
+      // offsets (a single thread must issue one MMA per 64 clocks to keep the
+      // tensor pipe full, so no descriptor arithmetic on the critical path).
+      // K-major SW128 tiles: K step kk sits at (kk/4) * 16 KB + (kk%4) * 32 B.
+      // MN-major V tile: K step kk (16 keys) sits at kk * 2 KB; N halves 16 KB apart.
+      // (The address field is the low 14 bits of (addr >> 4); every operand lies
+      // below 256 KB, so adding an address delta >> 4 never carries out of it.)
+      const uint64_t q_desc0 = smem_desc(sQ, 16, 1024);
+      const uint64_t k_desc0 = smem_desc(sK, 16, 1024);
+      const uint64_t v_desc0 = smem_desc(sV, kHalfBytes, 1024);
       // S_t = Q_t K_j^T : 8 MMAs of K=16 over the 128 head dims.
       auto issue_s = [&](int t, int j) {
-        const uint32_t q_base = sQ + t * kTileBytes;
-        const uint32_t k_base = sK + (j % kKStages) * kTileBytes;
+        const uint64_t qd = q_desc0 + (uint64_t)((t * kTileBytes) >> 4);
+        const uint64_t kd = k_desc0 + (uint64_t)(((j % kKStages) * kTileBytes) >> 4);
+        const uint32_t d = tmem + kTmemS + t * 128;
 #pragma unroll
         for (int kk = 0; kk < kHeadDim / 16; ++kk) {
-          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          mma_ss(tmem + kTmemS + t * 128, smem_desc(q_base + off, 16, 1024),
-                 smem_desc(k_base + off, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
+          const uint64_t off = (uint64_t)(((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4);
+          mma_ss(d, qd + off, kd + off, idesc_qk, kk > 0 ? 1u : 0u);
         }
       };
-      // O_t += P_t V_j : 8 MMAs of K=16 over the 128 keys of the block.
-      auto issue_pv = [&](int t, int j) {
-        const uint32_t v_base = sV + (j % kVStages) * kTileBytes;
+      // O_t += P_t V_j over keys [64h, 64h+64): 4 MMAs of K=16.
+      auto issue_pv = [&](int t, int j, int h) {
+        const uint64_t vd = v_desc0 + (uint64_t)(((j % kVStages) * kTileBytes) >> 4);
+        const uint32_t d = tmem + kTmemO + t * 128;
+        const uint32_t a = tmem + kTmemS + t * 128 + h * 64;
 #pragma unroll
-        for (int kk = 0; kk < kBlockN / 16; ++kk) {
-          mma_ts(tmem + kTmemO + t * 128, tmem + kTmemS + t * 128 + kk * 8,
-                 smem_desc(v_base + kk * 2048, kHalfBytes, 1024), idesc_pv,
+        for (int k4 = 0; k4 < kBlockN / 32; ++k4) {
+          const int kk = h * (kBlockN / 32) + k4;
+          mma_ts(d, a + k4 * 8, vd + (uint64_t)((kk * 2048) >> 4), idesc_pv,
                  (j > 0 || kk > 0) ? 1u : 0u);
         }
       };
@@ -420,14 +530,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       for (int j = 0; j < n_kv && ok; ++j) {
         for (int t = 0; t < kTiles && ok; ++t) {
-          ok = wait_bar(bar_p(t), j & 1, abort_flag, prm.status);
+          ok = wait_bar(bar_p(t, 0), j & 1, abort_flag, prm.status);
           if (!ok) break;
           if (t == 0) {
             ok = wait_bar(bar_vfull(j % kVStages), (j / kVStages) & 1, abort_flag, prm.status);
             if (!ok) break;
           }
           tc_fence_after();
-          issue_pv(t, j);
+          issue_pv(t, j, 0);
+          ok = wait_bar(bar_p(t, 1), j & 1, abort_flag, prm.status);
+          if (!ok) break;
+          tc_fence_after();
+          issue_pv(t, j, 1);
           if (t == kTiles - 1) mma_commit(bar_vempty(j % kVStages));
           if (j + 1 < n_kv) {
             if (t == 0) {
@@ -446,97 +560,133 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- softmax warpgroups ----------------
-    const int t = warp >> 2;                 // query tile of this warpgroup
-    const int lane_base = (warp & 3) * 32;   // TMEM lanes owned by this warp
-    const int row_in_tile = lane_base + lane;
-    const uint32_t t_s = tmem + ((uint32_t)lane_base << 16) + kTmemS + t * 128;
-    const uint32_t t_o = tmem + ((uint32_t)lane_base << 16) + kTmemO + t * 128;
+    // ---------------- softmax: 8 warps per query tile ----------------
+    const int t = warp >> 3;         // query tile
+    const int quad = warp & 3;       // TMEM lane quadrant: rows 32*quad .. +31
+    const int hk = (warp >> 2) & 1;  // key half [64hk, 64hk+64) of every block
+    const int row_in_tile = quad * 32 + lane;
+    const uint32_t lanes = (uint32_t)(quad * 32) << 16;
+    const uint32_t t_s = tmem + lanes + kTmemS + t * 128 + hk * 64;  // this warp's S columns
+    const uint32_t t_o = tmem + lanes + kTmemO + t * 128 + hk * 64;  // this warp's O columns
+    float* xch = reinterpret_cast<float*>(smem + kSmemXch);
+    auto xslot = [&](int parity, int half) {
+      return xch + ((t * 2 + parity) * 2 + half) * kBlockM + row_in_tile;
+    };
+    const uint32_t pair_bar = 1 + t * 4 + quad;  // named barrier of the two warps on these rows
     const float c = prm.scale_log2;
     float m_use = -INFINITY;
     float l_sum = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv; ++j) {
       ok = wait_bar(bar_s(t), j & 1, abort_flag, prm.status);
-      // tcgen05.ld/st below are warp-collective: leave together or not at all.
+      // tcgen05.ld/st below are warp-collective; the named barrier is pair-collective.
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      uint32_t s[4][32];
+      const int valid = prm.seq_k - j * kBlockN - hk * 64;  // keys of this half that exist
+      // Pass 1: max over this warp's 64 columns, then combine with the partner.
+      float mx;
+      {
+        uint32_t a[32], b[32];
+        tmem_ld32(t_s, a);
+        tmem_ld32(t_s + 32, b);
+        tmem_ld_wait(a);
+        tmem_pin(b);
+        if (valid < 64) {
+          mask_keys(a, 0, valid);
+          mask_keys(b, 32, valid);
+        }
+        float mxp[8];
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) tmem_ld32(t_s + q4 * 32, s[q4]);
-      tmem_ld_wait(s[0]);
-      tmem_pin(s[1]);
-      tmem_pin(s[2]);
-      tmem_pin(s[3]);
-      const int valid = prm.seq_k - j * kBlockN;  // keys of this block that exist
-      if (valid < kBlockN) {
+        for (int i = 0; i < 8; ++i)
+          mxp[i] = max3(__uint_as_float(a[4 * i]), __uint_as_float(a[4 * i + 1]),
+                        __uint_as_float(a[4 * i + 2]));
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4)
-#pragma unroll
-          for (int i = 0; i < 32; ++i)
-            if (q4 * 32 + i >= valid) s[q4][i] = __float_as_uint(-INFINITY);
+        for (int i = 0; i < 8; ++i) {
+          mxp[i] = max3(mxp[i], __uint_as_float(a[4 * i + 3]), __uint_as_float(b[4 * i]));
+          mxp[i] = max3(mxp[i], __uint_as_float(b[4 * i + 1]), __uint_as_float(b[4 * i + 2]));
+          mxp[i] = fmaxf(mxp[i], __uint_as_float(b[4 * i + 3]));
+        }
+        mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
+                   fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
       }
-      // Row max with 8 independent chains (a single chain is latency-bound).
-      float mxp[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mxp[i] = -INFINITY;
-#pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4)
-#pragma unroll
-        for (int i = 0; i < 32; ++i) mxp[i & 7] = fmaxf(mxp[i & 7], __uint_as_float(s[q4][i]));
-      const float mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                             fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
+      *xslot(j & 1, hk) = mx;
+      named_bar_sync(pair_bar, 64);
+      mx = fmaxf(mx, *xslot(j & 1, hk ^ 1));
       const float m_new = mx * c;
-      const bool need = m_new > m_use + kRescaleThreshold;
+      const bool need = m_new > m_use + kRescaleThreshold;  // same in both warps of the pair
       // tcgen05.ld/st are warp-collective: the whole warp rescales if any row must.
       if (j > 0 && __any_sync(0xffffffffu, need)) {
         // PV_t(j-1) is complete: the S_t(j) commit covers every earlier MMA.
         const float alpha = need ? ex2(m_use - m_new) : 1.f;
 #pragma unroll 1
-        for (int q4 = 0; q4 < 4; ++q4) {
+        for (int q2 = 0; q2 < 2; ++q2) {
           uint32_t o[32];
-          tmem_ld32(t_o + q4 * 32, o);
+          tmem_ld32(t_o + q2 * 32, o);
           tmem_ld_wait(o);
 #pragma unroll
           for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(t_o + q4 * 32, o);
+          tmem_st32(t_o + q2 * 32, o);
         }
         l_sum *= alpha;
       }
       if (need) m_use = m_new;
-      const float neg_m = -m_use;
-      float lp[4] = {0.f, 0.f, 0.f, 0.f};
+      // Pass 2: p = 2^(s*c - m) in 16-column chunks, the next chunk's tcgen05.ld
+      // in flight while this one is exponentiated. Column pairs run in packed
+      // fp32x2; kPolyPairs of every 8 pairs use the FMA-pipe exp2 so the MUFU
+      // and FMA pipes share the exponentials. P (bf16) of chunk q goes to S
+      // columns [8q, 8q+8) of this warp's range, which pass 2 has already read.
+      const float2 c2 = make_float2(c, c);
+      const float2 nm2 = make_float2(-m_use, -m_use);
+      float2 lp[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      uint32_t sb[2][16];
+      tmem_ld16(t_s, sb[0]);
+      tmem_ld_wait16(sb[0]);
 #pragma unroll
-      for (int q4 = 0; q4 < 4; ++q4) {
-        uint32_t pk[16];
+      for (int q = 0; q < 4; ++q) {
+        uint32_t(&cur)[16] = sb[q & 1];
+        if (q < 3) tmem_ld16(t_s + (q + 1) * 16, sb[(q + 1) & 1]);
+        if (valid < 64) mask_keys16(cur, q * 16, valid);
+        uint32_t pk[8];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float p0 = ex2(fmaf(__uint_as_float(s[q4][2 * i]), c, neg_m));
-          const float p1 = ex2(fmaf(__uint_as_float(s[q4][2 * i + 1]), c, neg_m));
-          lp[i & 3] += p0 + p1;
-          pk[i] = pack_bf16(p0, p1);
+        for (int i = 0; i < 8; ++i) {
+          const float2 x = __ffma2_rn(
+              make_float2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1])), c2, nm2);
+          float2 p;
+          if (((q * 8 + i) & 7) >= 8 - kPolyPairs) {
+            p = exp2_poly(x);
+          } else {
+            p.x = ex2(x.x);
+            p.y = ex2(x.y);
+          }
+          lp[i & 1] = __fadd2_rn(lp[i & 1], p);
+          pk[i] = pack_bf16(p.x, p.y);
         }
-        tmem_st16(t_s + q4 * 16, pk);
+        tmem_st8(t_s + q * 8, pk);
+        if (q < 3) tmem_ld_wait16(sb[(q + 1) & 1]);
       }
-      l_sum += (lp[0] + lp[1]) + (lp[2] + lp[3]);
       tmem_st_wait();
       tc_fence_before();
-      mbar_arrive(bar_p(t));
+      mbar_arrive(bar_p(t, hk));
+      l_sum += (lp[0].x + lp[0].y) + (lp[1].x + lp[1].y);
     }
     // ---------------- epilogue: O / l -> bf16 -> global ----------------
     if (ok) ok = wait_bar(bar_o(t), 0, abort_flag, prm.status);
     ok = __all_sync(0xffffffffu, ok);
     if (ok) {
       tc_fence_after();
+      // Row sum = both halves' shares (the parity after the last max exchange).
+      *xslot(n_kv & 1, hk) = l_sum;
+      named_bar_sync(pair_bar, 64);
+      const float inv_l = 1.f / (l_sum + *xslot(n_kv & 1, hk ^ 1));
       const int row = q_row0 + t * kBlockM + row_in_tile;
-      const float inv_l = 1.f / l_sum;
       __nv_bfloat16* dst = prm.out + (int64_t)batch * prm.o_batch_stride +
-                           (int64_t)row * prm.o_row_stride + (int64_t)head * prm.o_head_stride;
+                           (int64_t)row * prm.o_row_stride + (int64_t)head * prm.o_head_stride +
+                           hk * 64;
 #pragma unroll 1
-      for (int q4 = 0; q4 < 4; ++q4) {
+      for (int q2 = 0; q2 < 2; ++q2) {
         uint32_t o[32];
-        tmem_ld32(t_o + q4 * 32, o);
+        tmem_ld32(t_o + q2 * 32, o);
         tmem_ld_wait(o);
         if (row < prm.seq_q) {
 #pragma unroll
@@ -550,7 +700,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             __uint_as_float(o[v8 * 8 + 5]) * inv_l);
             u.w = pack_bf16(__uint_as_float(o[v8 * 8 + 6]) * inv_l,
                             __uint_as_float(o[v8 * 8 + 7]) * inv_l);
-            *reinterpret_cast<uint4*>(dst + q4 * 32 + v8 * 8) = u;
+            *reinterpret_cast<uint4*>(dst + q2 * 32 + v8 * 8) = u;
           }
         }
       }

@@ -85,6 +85,12 @@ __device__ __forceinline__ void norm_rope_chunk(float (&v)[8], const __nv_bfloat
   }
 }
 
+// Both kernels below flatten their work into head rows; a group of L = D/8
+// lanes owns one head row per item and every thread keeps kItems items in
+// flight (all loads issued before the first reduction) so enough bytes are
+// outstanding per SM to cover HBM latency.
+constexpr int kItems = 4;
+
 // ---- standalone fused_qknorm_rope: x, out contiguous [B*S*H, D] -------------
 
 template <int D, bool kShuffle>
@@ -95,28 +101,38 @@ __global__ void __launch_bounds__(256) qknorm_rope_kernel(__nv_bfloat16* out,
                                                          int64_t nrows, int64_t heads,
                                                          int64_t seq, int rot, float eps) {
   constexpr int L = D / 8;
-  constexpr int kRowsPerCta = 256 / L;
-  __shared__ float smem[kShuffle ? 1 : kRowsPerCta * D];
+  constexpr int G = 256 / L;  // head rows per CTA pass
+  __shared__ float smem[kShuffle ? 1 : G * D];
   const int sub = threadIdx.x % L;
   const int slot = threadIdx.x / L;
-  const int64_t hr = (int64_t)blockIdx.x * kRowsPerCta + slot;
-  const bool active = hr < nrows;
-  const int64_t hr_c = active ? hr : nrows - 1;  // keep every lane in the shuffles
-  const int64_t token = (hr_c / heads) % seq;
-  float v[8];
-  f8 in = unpack8(ld_stream(x + hr_c * D + sub * 8));
+  const int64_t base = (int64_t)blockIdx.x * G * kItems;
+  uint4 raw[kItems];
 #pragma unroll
-  for (int j = 0; j < 8; ++j) v[j] = in.v[j];
-  norm_rope_chunk<D, kShuffle>(v, weight, cos + token * rot, sin + token * rot, rot, eps, sub,
-                               kShuffle ? nullptr : smem + slot * D);
-  if (active) st_stream(out + hr * D + sub * 8, pack8(v));
+  for (int k = 0; k < kItems; ++k) {
+    const int64_t hr = base + k * G + slot;
+    const int64_t hr_c = hr < nrows ? hr : nrows - 1;  // inactive lanes still join the shuffles
+    raw[k] = ld_stream(x + hr_c * D + sub * 8);
+  }
+#pragma unroll
+  for (int k = 0; k < kItems; ++k) {
+    const int64_t hr = base + k * G + slot;
+    const int64_t hr_c = hr < nrows ? hr : nrows - 1;
+    const int64_t token = (hr_c / heads) % seq;
+    f8 in = unpack8(raw[k]);
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) v[j] = in.v[j];
+    norm_rope_chunk<D, kShuffle>(v, weight, cos + token * rot, sin + token * rot, rot, eps, sub,
+                                 kShuffle ? nullptr : smem + slot * D);
+    if (hr < nrows) st_stream(out + hr * D + sub * 8, pack8(v));
+  }
 }
 
 // ---- fused q/k norm + rope + destination-major pack -------------------------
 //
-// One CTA per token row. Work items are the 3*H head rows of that token
-// (q heads, k heads, v heads); each group of L lanes takes items slot,
-// slot+G, ... (G = 256/L head rows in flight per CTA pass).
+// Work items are the rows * 3H head rows (row-major: q heads, k heads, v heads
+// of token 0, then token 1, ...). Each group of L lanes takes kItems items
+// spaced G apart.
 template <int D, bool kShuffle>
 __global__ void __launch_bounds__(256) qknorm_rope_pack_kernel(
     __nv_bfloat16* send, const __nv_bfloat16* q, const __nv_bfloat16* k,
@@ -128,34 +144,48 @@ __global__ void __launch_bounds__(256) qknorm_rope_pack_kernel(
   __shared__ float smem[kShuffle ? 1 : G * D];
   const int sub = threadIdx.x % L;
   const int slot = threadIdx.x / L;
-  const int64_t row = blockIdx.x;
-  const float* cos_row = cos + row * rot;
-  const float* sin_row = sin + row * rot;
-  const int items = 3 * heads;
-  for (int it0 = 0; it0 < items; it0 += G) {
-    const int it = it0 + slot;
-    const bool active = it < items;
-    const int itc = active ? it : items - 1;
-    const int part = itc / heads;  // 0 = q, 1 = k, 2 = v (uniform per head row)
-    const int g = itc - part * heads;
-    const __nv_bfloat16* src =
-        part == 0 ? q + row * q_stride : (part == 1 ? k + row * k_stride : v + row * v_stride);
-    const uint4 raw = ld_stream(src + (int64_t)g * D + sub * 8);
-    f8 in = unpack8(raw);
+  const int per_row = 3 * heads;
+  const int64_t total = rows * per_row;
+  const int64_t base = (int64_t)blockIdx.x * G * kItems;
+  uint4 raw[kItems];
+  int row_of[kItems], item_of[kItems];
+#pragma unroll
+  for (int it = 0; it < kItems; ++it) {
+    int64_t w = base + it * G + slot;
+    if (w >= total) w = total - 1;  // inactive lanes still join the shuffles
+    const int w32 = (int)w;  // total < 2^31 (checked by the launcher)
+    const int row = w32 / per_row;
+    const int item = w32 - row * per_row;
+    row_of[it] = row;
+    item_of[it] = item;
+    const int part = item / heads;
+    const int g = item - part * heads;
+    const __nv_bfloat16* src = part == 0   ? q + row * q_stride
+                               : part == 1 ? k + row * k_stride
+                                           : v + row * v_stride;
+    raw[it] = ld_stream(src + (int64_t)g * D + sub * 8);
+  }
+#pragma unroll
+  for (int it = 0; it < kItems; ++it) {
+    const int64_t w = base + it * G + slot;
+    const int row = row_of[it];
+    const int part = item_of[it] / heads;  // 0 = q, 1 = k, 2 = v
+    const int g = item_of[it] - part * heads;
+    f8 in = unpack8(raw[it]);
     // Head rows of different parts share a warp: the warp-collective norm runs
     // for every lane and v rows store their raw bits unchanged.
     float nv[8];
 #pragma unroll
     for (int j = 0; j < 8; ++j) nv[j] = in.v[j];
-    norm_rope_chunk<D, kShuffle>(nv, part == 1 ? wk : wq, cos_row, sin_row, rot,
-                                 part == 1 ? k_eps : q_eps, sub,
+    norm_rope_chunk<D, kShuffle>(nv, part == 1 ? wk : wq, cos + (int64_t)row * rot,
+                                 sin + (int64_t)row * rot, rot, part == 1 ? k_eps : q_eps, sub,
                                  kShuffle ? nullptr : smem + slot * D);
-    if (active) {
+    if (w < total) {
       const int dst = g / hl;
       const int lh = g - dst * hl;
       __nv_bfloat16* o =
           send + (((int64_t)dst * rows + row) * hl + lh) * (3 * D) + part * D + sub * 8;
-      st_stream(o, part == 2 ? raw : pack8(nv));
+      st_stream(o, part == 2 ? raw[it] : pack8(nv));
     }
   }
 }
@@ -238,7 +268,7 @@ template <int D, bool kShuffle>
 void launch_qkrope(__nv_bfloat16* out, const __nv_bfloat16* x, const __nv_bfloat16* w,
                    const float* cos, const float* sin, int64_t nrows, int64_t heads,
                    int64_t seq, int rot, float eps, cudaStream_t s) {
-  constexpr int kRowsPerCta = 256 / (D / 8);
+  constexpr int kRowsPerCta = 256 / (D / 8) * kItems;
   const int64_t grid = (nrows + kRowsPerCta - 1) / kRowsPerCta;
   qknorm_rope_kernel<D, kShuffle><<<(unsigned)grid, 256, 0, s>>>(out, x, w, cos, sin, nrows,
                                                                  heads, seq, rot, eps);
@@ -302,7 +332,7 @@ extern "C" int h3b_qknorm_rope_pack(void* send, const void* q, const void* k, co
     return H3B_ERR_UNSUPPORTED;
   }
   if (rows == 0) return H3B_OK;
-  H3B_REQUIRE(rows <= 0x7fffffffLL, "qknorm_rope_pack: too many rows");
+  H3B_REQUIRE(rows * 3 * heads <= 0x7fffffffLL, "qknorm_rope_pack: too many rows");
   H3B_REQUIRE(aligned16(send) && aligned16(q) && aligned16(k) && aligned16(v) &&
                   aligned16(q_weight) && aligned16(k_weight) && q_row_stride % 8 == 0 &&
                   k_row_stride % 8 == 0 && v_row_stride % 8 == 0,
@@ -311,8 +341,10 @@ extern "C" int h3b_qknorm_rope_pack(void* send, const void* q, const void* k, co
   const bool shuffle = rotary_dim % 16 == 0 && aligned16(cos) && aligned16(sin);
   const int hl = (int)(heads / world);
   auto* o = (__nv_bfloat16*)send;
+  const int64_t total_items = rows * 3 * heads;
 #define H3B_QKP(DD, SH)                                                                   \
-  h3b::qknorm_rope_pack_kernel<DD, SH><<<(unsigned)rows, 256, 0, stream>>>(                 \
+  h3b::qknorm_rope_pack_kernel<DD, SH><<<(unsigned)((total_items + (256 / (DD / 8)) * h3b::kItems - 1) / \
+                                           ((256 / (DD / 8)) * h3b::kItems)), 256, 0, stream>>>(   \
       o, (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,        \
       q_row_stride, k_row_stride, v_row_stride, (const __nv_bfloat16*)q_weight,            \
       (const __nv_bfloat16*)k_weight, cos, sin, rows, (int)heads, hl, (int)rotary_dim,     \
