@@ -21,7 +21,7 @@ H3B_OK = 0
 H3B_ERR_VALUE = 1
 H3B_ERR_CUDA = 2
 H3B_ERR_UNSUPPORTED = 3
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -43,7 +43,8 @@ SIGNATURES: dict[str, list[Any]] = {
     "h3b_pack_qkv": [_p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64, _i64,
                      _i64, _p],
     "h3b_merge_heads": [_p, _p, _i64, _i64, _i64, _p],
-    "h3b_attention": [_p, _p, _p, _p] + [_i64] * 17 + [_f32, _p],
+    "h3b_attention": [_p, _p, _p, _p] + [_i64] * 17 + [_f32, _p, _i64, _p],
+    "h3b_attention_workspace_size": [_i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_i64)],
     "h3b_clear_device_status": [_p],
 }
 
@@ -105,7 +106,7 @@ def check(code: int, what: str) -> None:
 
 
 _LAUNCHES = 0
-_NON_KERNEL = {"h3b_clear_device_status"}
+_NON_KERNEL = {"h3b_clear_device_status", "h3b_attention_workspace_size"}
 
 
 def call(name: str, *args: Any) -> None:

@@ -379,7 +379,17 @@ struct Params {
   int seq_q, seq_k;
   float scale_log2;  // softmax_scale * log2(e)
   unsigned int* status;
+  // Work decomposition. A unit is (batch, head, 256-row query block). Units
+  // [0, n_full) run whole; each later unit runs as `splits` CTAs over
+  // consecutive key ranges of `blocks_per_split` blocks, writing unnormalised
+  // fp32 O and (max, sum) per row to `ws` for attention_combine.
+  int heads, units_per_bh, n_full, splits, blocks_per_split;
+  float* ws;
 };
+
+// Workspace floats per split CTA: per tile, O [128 x 128] then (m, l) [128 x 2].
+constexpr int kWsTileFloats = kBlockM * kHeadDim + 2 * kBlockM;
+constexpr int kWsSlotFloats = kTiles * kWsTileFloats;
 
 __global__ void __launch_bounds__(kThreads, 1)
     attention_fwd(const __grid_constant__ CUtensorMap q_map,
@@ -411,10 +421,20 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int head = blockIdx.y;
-  const int batch = blockIdx.z;
-  const int q_row0 = blockIdx.x * (kTiles * kBlockM);
-  const int n_kv = (prm.seq_k + kBlockN - 1) / kBlockN;
+  const int n_kv_total = (prm.seq_k + kBlockN - 1) / kBlockN;
+  int unit = blockIdx.x, j0 = 0, n_kv = n_kv_total, split_slot = -1;
+  if ((int)blockIdx.x >= prm.n_full) {
+    const int r = blockIdx.x - prm.n_full;
+    unit = prm.n_full + r / prm.splits;
+    j0 = (r % prm.splits) * prm.blocks_per_split;
+    n_kv = min(n_kv_total - j0, prm.blocks_per_split);
+    split_slot = r;
+  }
+  const int qb = unit % prm.units_per_bh;
+  const int bh = unit / prm.units_per_bh;
+  const int head = bh % prm.heads;
+  const int batch = bh / prm.heads;
+  const int q_row0 = qb * (kTiles * kBlockM);
 
   if (threadIdx.x == 0) {
     for (int t = 0; t < kTiles; ++t) {
@@ -469,14 +489,15 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!ok) break;
         mbar_expect_tx(bar_kfull(ks), kTileBytes);
         const uint32_t kdst = sK + ks * kTileBytes;
-        tma_load_4d(kdst, &k_map, bar_kfull(ks), 0, head, j * kBlockN, batch);
-        tma_load_4d(kdst + kHalfBytes, &k_map, bar_kfull(ks), 64, head, j * kBlockN, batch);
+        const int key0 = (j0 + j) * kBlockN;
+        tma_load_4d(kdst, &k_map, bar_kfull(ks), 0, head, key0, batch);
+        tma_load_4d(kdst + kHalfBytes, &k_map, bar_kfull(ks), 64, head, key0, batch);
         ok = wait_bar(bar_vempty(vs), ((j / kVStages) & 1) ^ 1, abort_flag, prm.status);
         if (!ok) break;
         mbar_expect_tx(bar_vfull(vs), kTileBytes);
         const uint32_t vdst = sV + vs * kTileBytes;
-        tma_load_4d(vdst, &v_map, bar_vfull(vs), 0, head, j * kBlockN, batch);
-        tma_load_4d(vdst + kHalfBytes, &v_map, bar_vfull(vs), 64, head, j * kBlockN, batch);
+        tma_load_4d(vdst, &v_map, bar_vfull(vs), 0, head, key0, batch);
+        tma_load_4d(vdst + kHalfBytes, &v_map, bar_vfull(vs), 64, head, key0, batch);
       }
     }
   } else if (warp == kMmaWarp) {
@@ -583,7 +604,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const int valid = prm.seq_k - j * kBlockN - hk * 64;  // keys of this half that exist
+      const int valid = prm.seq_k - (j0 + j) * kBlockN - hk * 64;  // keys of this half that exist
       // Pass 1: max over this warp's 64 columns, then combine with the partner.
       float mx;
       {
@@ -678,29 +699,52 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Row sum = both halves' shares (the parity after the last max exchange).
       *xslot(n_kv & 1, hk) = l_sum;
       named_bar_sync(pair_bar, 64);
-      const float inv_l = 1.f / (l_sum + *xslot(n_kv & 1, hk ^ 1));
-      const int row = q_row0 + t * kBlockM + row_in_tile;
-      __nv_bfloat16* dst = prm.out + (int64_t)batch * prm.o_batch_stride +
-                           (int64_t)row * prm.o_row_stride + (int64_t)head * prm.o_head_stride +
-                           hk * 64;
+      const float l_row = l_sum + *xslot(n_kv & 1, hk ^ 1);
+      if (split_slot >= 0) {
+        // Partial result of a key range: unnormalised O and (running max, sum).
+        float* ws = prm.ws + (int64_t)split_slot * kWsSlotFloats + t * kWsTileFloats;
+        float* o_row = ws + row_in_tile * kHeadDim + hk * 64;
 #pragma unroll 1
-      for (int q2 = 0; q2 < 2; ++q2) {
-        uint32_t o[32];
-        tmem_ld32(t_o + q2 * 32, o);
-        tmem_ld_wait(o);
-        if (row < prm.seq_q) {
+        for (int q2 = 0; q2 < 2; ++q2) {
+          uint32_t o[32];
+          tmem_ld32(t_o + q2 * 32, o);
+          tmem_ld_wait(o);
 #pragma unroll
-          for (int v8 = 0; v8 < 4; ++v8) {
-            uint4 u;
-            u.x = pack_bf16(__uint_as_float(o[v8 * 8 + 0]) * inv_l,
-                            __uint_as_float(o[v8 * 8 + 1]) * inv_l);
-            u.y = pack_bf16(__uint_as_float(o[v8 * 8 + 2]) * inv_l,
-                            __uint_as_float(o[v8 * 8 + 3]) * inv_l);
-            u.z = pack_bf16(__uint_as_float(o[v8 * 8 + 4]) * inv_l,
-                            __uint_as_float(o[v8 * 8 + 5]) * inv_l);
-            u.w = pack_bf16(__uint_as_float(o[v8 * 8 + 6]) * inv_l,
-                            __uint_as_float(o[v8 * 8 + 7]) * inv_l);
-            *reinterpret_cast<uint4*>(dst + q2 * 32 + v8 * 8) = u;
+          for (int v4 = 0; v4 < 8; ++v4)
+            *reinterpret_cast<float4*>(o_row + q2 * 32 + v4 * 4) =
+                make_float4(__uint_as_float(o[v4 * 4 + 0]), __uint_as_float(o[v4 * 4 + 1]),
+                            __uint_as_float(o[v4 * 4 + 2]), __uint_as_float(o[v4 * 4 + 3]));
+        }
+        if (hk == 0) {
+          float* ml = ws + kBlockM * kHeadDim + 2 * row_in_tile;
+          ml[0] = m_use;
+          ml[1] = l_row;
+        }
+      } else {
+        const float inv_l = 1.f / l_row;
+        const int row = q_row0 + t * kBlockM + row_in_tile;
+        __nv_bfloat16* dst = prm.out + (int64_t)batch * prm.o_batch_stride +
+                             (int64_t)row * prm.o_row_stride +
+                             (int64_t)head * prm.o_head_stride + hk * 64;
+#pragma unroll 1
+        for (int q2 = 0; q2 < 2; ++q2) {
+          uint32_t o[32];
+          tmem_ld32(t_o + q2 * 32, o);
+          tmem_ld_wait(o);
+          if (row < prm.seq_q) {
+#pragma unroll
+            for (int v8 = 0; v8 < 4; ++v8) {
+              uint4 u;
+              u.x = pack_bf16(__uint_as_float(o[v8 * 8 + 0]) * inv_l,
+                              __uint_as_float(o[v8 * 8 + 1]) * inv_l);
+              u.y = pack_bf16(__uint_as_float(o[v8 * 8 + 2]) * inv_l,
+                              __uint_as_float(o[v8 * 8 + 3]) * inv_l);
+              u.z = pack_bf16(__uint_as_float(o[v8 * 8 + 4]) * inv_l,
+                              __uint_as_float(o[v8 * 8 + 5]) * inv_l);
+              u.w = pack_bf16(__uint_as_float(o[v8 * 8 + 6]) * inv_l,
+                              __uint_as_float(o[v8 * 8 + 7]) * inv_l);
+              *reinterpret_cast<uint4*>(dst + q2 * 32 + v8 * 8) = u;
+            }
           }
         }
       }
@@ -715,6 +759,92 @@ __global__ void __launch_bounds__(kThreads, 1)
                  "r"(kTmemCols)
                  : "memory");
   }
+}
+
+
+// Merges the key-range partials of the split units: one warp per query row,
+// 4 head dims per lane. O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.
+__global__ void __launch_bounds__(256) attention_combine(const Params prm, int split_units) {
+  const int gw = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  constexpr int kRowsPerUnit = kTiles * kBlockM;
+  if (gw >= split_units * kRowsPerUnit) return;
+  const int ui = gw / kRowsPerUnit;
+  const int rr = gw - ui * kRowsPerUnit;
+  const int t = rr / kBlockM;
+  const int r_in_tile = rr - t * kBlockM;
+  const int unit = prm.n_full + ui;
+  const int qb = unit % prm.units_per_bh;
+  const int bh = unit / prm.units_per_bh;
+  const int head = bh % prm.heads;
+  const int batch = bh / prm.heads;
+  const int row = qb * kRowsPerUnit + rr;
+  if (row >= prm.seq_q) return;
+  auto tile_ws = [&](int split) {
+    return prm.ws + (int64_t)(ui * prm.splits + split) * kWsSlotFloats + t * kWsTileFloats;
+  };
+  float m_max = -INFINITY;
+  for (int sp = 0; sp < prm.splits; ++sp)
+    m_max = fmaxf(m_max, tile_ws(sp)[kBlockM * kHeadDim + 2 * r_in_tile]);
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  float l_tot = 0.f;
+  for (int sp = 0; sp < prm.splits; ++sp) {
+    const float* w = tile_ws(sp);
+    const float scale = ex2(w[kBlockM * kHeadDim + 2 * r_in_tile] - m_max);
+    l_tot += scale * w[kBlockM * kHeadDim + 2 * r_in_tile + 1];
+    const float4 o = *reinterpret_cast<const float4*>(w + r_in_tile * kHeadDim + lane * 4);
+    acc.x += scale * o.x;
+    acc.y += scale * o.y;
+    acc.z += scale * o.z;
+    acc.w += scale * o.w;
+  }
+  const float inv = 1.f / l_tot;
+  __nv_bfloat16* dst = prm.out + (int64_t)batch * prm.o_batch_stride +
+                       (int64_t)row * prm.o_row_stride + (int64_t)head * prm.o_head_stride +
+                       lane * 4;
+  uint2 u;
+  u.x = pack_bf16(acc.x * inv, acc.y * inv);
+  u.y = pack_bf16(acc.z * inv, acc.w * inv);
+  *reinterpret_cast<uint2*>(dst) = u;
+}
+
+// Work plan of one call: which units run whole and how the last, partial wave
+// of units is split along the keys so that it fills the GPU.
+struct Plan {
+  int units_per_bh, units, n_full, splits, blocks_per_split, grid, split_units;
+  int64_t ws_bytes;
+};
+
+Plan make_plan(int64_t batch, int64_t seq_q, int64_t seq_k, int64_t heads) {
+  Plan pl{};
+  pl.units_per_bh = (int)((seq_q + kTiles * kBlockM - 1) / (kTiles * kBlockM));
+  pl.units = (int)(pl.units_per_bh * heads * batch);
+  const int n_kv = (int)((seq_k + kBlockN - 1) / kBlockN);
+  const int sms = num_sms();
+  const int rem = pl.units % sms;
+  pl.splits = 1;
+  pl.blocks_per_split = n_kv;
+  if (rem > 0 && 2 * rem <= sms && n_kv >= 2) {
+    int want = sms / rem;
+    if (want > 32) want = 32;
+    if (want > n_kv) want = n_kv;
+    pl.blocks_per_split = (n_kv + want - 1) / want;
+    pl.splits = (n_kv + pl.blocks_per_split - 1) / pl.blocks_per_split;
+  }
+  if (pl.splits >= 2) {
+    pl.split_units = rem;
+    pl.n_full = pl.units - rem;
+    pl.grid = pl.n_full + rem * pl.splits;
+    pl.ws_bytes = (int64_t)rem * pl.splits * kWsSlotFloats * (int64_t)sizeof(float);
+  } else {
+    pl.splits = 1;
+    pl.blocks_per_split = n_kv;
+    pl.split_units = 0;
+    pl.n_full = pl.units;
+    pl.grid = pl.units;
+    pl.ws_bytes = 0;
+  }
+  return pl;
 }
 
 // ---------------------------------------------------------------------------
@@ -775,7 +905,7 @@ extern "C" int h3b_attention(void* out, const void* q, const void* k, const void
                              int64_t v_batch_stride, int64_t v_row_stride,
                              int64_t v_head_stride, int64_t o_batch_stride,
                              int64_t o_row_stride, int64_t o_head_stride, float softmax_scale,
-                             h3b_stream_t stream) {
+                             void* workspace, int64_t workspace_bytes, h3b_stream_t stream) {
   using namespace h3b::attn;
   H3B_REQUIRE(batch >= 0 && seq_q >= 0 && seq_k >= 0 && heads >= 0,
               "attention: negative shape");
@@ -785,7 +915,8 @@ extern "C" int h3b_attention(void* out, const void* q, const void* k, const void
   }
   if (batch == 0 || seq_q == 0 || heads == 0) return H3B_OK;
   H3B_REQUIRE(seq_k > 0, "attention: empty key sequence");
-  H3B_REQUIRE(batch <= 65535 && heads <= 65535 && seq_q < (1LL << 31) && seq_k < (1LL << 31),
+  H3B_REQUIRE(seq_q < (1LL << 31) && seq_k < (1LL << 31) &&
+                  ((seq_q + 255) / 256) * heads * batch < (1LL << 31),
               "attention: shape exceeds launch limits");
   H3B_REQUIRE(h3b::aligned16(q) && h3b::aligned16(k) && h3b::aligned16(v) &&
                   h3b::aligned16(out),
@@ -824,6 +955,16 @@ extern "C" int h3b_attention(void* out, const void* q, const void* k, const void
       if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
   }
+  Plan pl = make_plan(batch, seq_q, seq_k, heads);
+  if (pl.ws_bytes > 0 && (workspace == nullptr || workspace_bytes < pl.ws_bytes ||
+                          !h3b::aligned16(workspace))) {
+    // No (or too small a) workspace: run every unit whole.
+    pl.splits = 1;
+    pl.split_units = 0;
+    pl.n_full = pl.grid = pl.units;
+    pl.blocks_per_split = (int)((seq_k + kBlockN - 1) / kBlockN);
+    pl.ws_bytes = 0;
+  }
   Params p;
   p.out = reinterpret_cast<__nv_bfloat16*>(out);
   p.o_batch_stride = o_batch_stride;
@@ -833,8 +974,31 @@ extern "C" int h3b_attention(void* out, const void* q, const void* k, const void
   p.seq_k = (int)seq_k;
   p.scale_log2 = (float)((double)softmax_scale * 1.4426950408889634);
   p.status = h3b::status_ptr();
-  dim3 grid((unsigned)((seq_q + kTiles * kBlockM - 1) / (kTiles * kBlockM)), (unsigned)heads,
-            (unsigned)batch);
-  attention_fwd<<<grid, kThreads, kSmemAlloc, stream>>>(qm, km, vm, p);
+  p.heads = (int)heads;
+  p.units_per_bh = pl.units_per_bh;
+  p.n_full = pl.n_full;
+  p.splits = pl.splits;
+  p.blocks_per_split = pl.blocks_per_split;
+  p.ws = reinterpret_cast<float*>(workspace);
+  attention_fwd<<<(unsigned)pl.grid, kThreads, kSmemAlloc, stream>>>(qm, km, vm, p);
+  if (pl.split_units > 0) {
+    int rc = h3b::check_launch("h3b_attention");
+    if (rc != H3B_OK) return rc;
+    const int warps = pl.split_units * kTiles * kBlockM;
+    attention_combine<<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>(p, pl.split_units);
+  }
   return h3b::check_launch("h3b_attention");
+}
+
+extern "C" int h3b_attention_workspace_size(int64_t batch, int64_t seq_q, int64_t seq_k,
+                                            int64_t heads, int64_t head_dim,
+                                            int64_t* bytes_out) {
+  using namespace h3b::attn;
+  H3B_REQUIRE(bytes_out != nullptr, "attention_workspace_size: null output pointer");
+  H3B_REQUIRE(batch >= 0 && seq_q >= 0 && seq_k >= 0 && heads >= 0,
+              "attention: negative shape");
+  *bytes_out = 0;
+  if (head_dim != kHeadDim || batch == 0 || seq_q == 0 || heads == 0 || seq_k == 0) return H3B_OK;
+  *bytes_out = make_plan(batch, seq_q, seq_k, heads).ws_bytes;
+  return H3B_OK;
 }

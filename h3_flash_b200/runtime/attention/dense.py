@@ -9,6 +9,7 @@ the ``[S, hl, D]`` layout the output all-to-all sends.
 
 from __future__ import annotations
 
+import ctypes
 import math
 
 import torch
@@ -46,11 +47,26 @@ def attention_bshd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         out = torch.empty((b, sq, h, d), dtype=q.dtype, device=q.device)
     _check_view("out", out)
     scale = float(softmax_scale) if softmax_scale is not None else 1.0 / math.sqrt(d)
+    ws_bytes = workspace_bytes(b, sq, k.shape[1], h, d)
+    # Scratch for the split tail (caller-owned: the C ABI never allocates).
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=q.device) if ws_bytes else None
     call("h3b_attention", ptr(out), ptr(q), ptr(k), ptr(v), b, sq, k.shape[1], h, d,
          q.stride(0), q.stride(1), q.stride(2), k.stride(0), k.stride(1), k.stride(2),
          v.stride(0), v.stride(1), v.stride(2), out.stride(0), out.stride(1), out.stride(2),
-         scale, stream_of(q))
+         scale, ptr(ws) if ws is not None else None, ws_bytes, stream_of(q))
     return out
+
+
+def workspace_bytes(batch: int, seq_q: int, seq_k: int, heads: int, head_dim: int = HEAD_DIM) -> int:
+    """Scratch bytes the attention call can use for this shape on the current device."""
+
+    from ... import _lib
+
+    value = ctypes.c_int64(0)
+    _lib.check(_lib.load().h3b_attention_workspace_size(batch, seq_q, seq_k, heads, head_dim,
+                                                         ctypes.byref(value)),
+               "h3b_attention_workspace_size")
+    return int(value.value)
 
 
 def packed_attention(packed: torch.Tensor, head_dim: int = HEAD_DIM,

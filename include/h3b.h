@@ -30,7 +30,7 @@ typedef struct CUstream_st* h3b_stream_t; /* == cudaStream_t */
 #define H3B_ERR_CUDA 2        /* CUDA launch or driver error: RuntimeError         */
 #define H3B_ERR_UNSUPPORTED 3 /* valid input this build does not handle: RuntimeError */
 
-#define H3B_ABI_VERSION 1
+#define H3B_ABI_VERSION 2
 
 int h3b_abi_version(void);
 /* Message of the last failing call on this host thread ("" if none). */
@@ -147,6 +147,12 @@ int h3b_merge_heads(void* out, const void* x, int64_t world, int64_t rows,
  * be a multiple of 8 elements and every base 16-byte aligned.
  * The packed-Ulysses receive buffer [S, hl, 3D] is the view
  *   q = qkv, k = qkv + D, v = qkv + 2D, row stride hl*3D, head stride 3D.
+ * Work is split into (batch, head, 256-query-row) units. When the last wave of
+ * units would leave SMs idle, those units are split along the keys and merged
+ * by a second kernel; that needs `workspace` (16-byte aligned, at least the
+ * size h3b_attention_workspace_size reports, caller-owned, only used during the
+ * call's kernels). With a null or short workspace every unit runs whole: same
+ * results, longer tail.
  * replaces torch SDPA at src/h3_flash/runtime/parallel/packed_ulysses.py:201-209 and
  *          flash_attn_func in src/h3_flash/runtime/attention/dense_fa4.py:74-81, :145
  * ------------------------------------------------------------------------- */
@@ -157,7 +163,13 @@ int h3b_attention(void* out, const void* q, const void* k, const void* v,
                   int64_t k_batch_stride, int64_t k_row_stride, int64_t k_head_stride,
                   int64_t v_batch_stride, int64_t v_row_stride, int64_t v_head_stride,
                   int64_t o_batch_stride, int64_t o_row_stride, int64_t o_head_stride,
-                  float softmax_scale, h3b_stream_t stream);
+                  float softmax_scale, void* workspace, int64_t workspace_bytes,
+                  h3b_stream_t stream);
+
+/* Bytes of workspace h3b_attention can use for this shape on the current
+ * device (0 if the shape needs none). Host-only; launches nothing. */
+int h3b_attention_workspace_size(int64_t batch, int64_t seq_q, int64_t seq_k, int64_t heads,
+                                 int64_t head_dim, int64_t* bytes_out);
 
 #ifdef __cplusplus
 }

@@ -27,7 +27,8 @@ def test_header_declares_the_hot_path():
     for expected in (
         "h3b_rmsnorm_modulate", "h3b_residual_gate_rmsnorm_modulate", "h3b_modulate", "h3b_gated_residual",
         "h3b_swiglu", "h3b_gelu_tanh", "h3b_qknorm_rope", "h3b_qknorm_rope_pack", "h3b_pack_qkv",
-        "h3b_merge_heads", "h3b_attention", "h3b_last_error", "h3b_abi_version",
+        "h3b_merge_heads", "h3b_attention", "h3b_attention_workspace_size", "h3b_last_error",
+        "h3b_abi_version",
     ):
         assert expected in names
 
@@ -57,11 +58,11 @@ def test_shape_errors_map_to_value_error_without_a_gpu():
 
 def test_unsupported_head_dim_is_a_runtime_error():
     with pytest.raises(RuntimeError, match="head_dim must be 128"):
-        _lib.call("h3b_attention", None, None, None, None, *([1] * 4), 64, *([64] * 12), 1.0, None)
+        _lib.call("h3b_attention", None, None, None, None, *([1] * 4), 64, *([64] * 12), 1.0, None, 0, None)
 
 
 def test_empty_inputs_are_noops():
     # rows == 0 returns before any launch
     _lib.call("h3b_swiglu", None, None, 0, 16, 32, 16, None)
     _lib.call("h3b_merge_heads", None, None, 2, 0, 128, None)
-    _lib.call("h3b_attention", None, None, None, None, 1, 0, 5, 1, 128, *([128] * 12), 1.0, None)
+    _lib.call("h3b_attention", None, None, None, None, 1, 0, 5, 1, 128, *([128] * 12), 1.0, None, 0, None)
