@@ -61,64 +61,70 @@ __global__ void __launch_bounds__(kRowWarps * 32) adaln_rows_vec(RowArgs a) {
   constexpr bool kTwoIn = (OP == kResRmsModulate || OP == kGatedResidual);
   constexpr bool kNorm = (OP == kRmsModulate || OP == kResRmsModulate);
 
-  float h[NCH][8];
-  uint4 raw0[NCH], raw1[NCH], rawg[NCH];
+  // The row stays in registers as packed bf16 (4 registers per 8 values); the
+  // fp32 values are recomputed from it where needed instead of being held, so a
+  // 3072-wide row costs ~50-100 registers and two CTAs fit per SM.
+  uint4 raw0[NCH], raw1[kTwoIn ? NCH : 1];
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const int col = (c * 32 + lane) * 8;
     if (col < cols) {
       raw0[c] = ld_stream(in0 + col);
-      if (kTwoIn) {
-        raw1[c] = ld_stream(in1 + col);
-        rawg[c] = ld_cached(gate + col);
-      }
+      if (kTwoIn) raw1[c] = ld_stream(in1 + col);
     }
   }
+  auto value = [&](int c, float (&h)[8]) {
+    const int col = (c * 32 + lane) * 8;
+    f8 x0 = unpack8(raw0[c]);
+    if (kTwoIn) {
+      f8 x1 = unpack8(raw1[c]);
+      f8 g = unpack8(ld_cached(gate + col));
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = x0.v[j] + g.v[j] * x1.v[j];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) h[j] = x0.v[j];
+    }
+  };
+
+  if (!kNorm) {
+    // Streaming ops: one pass, output straight from the loaded chunk.
+    __nv_bfloat16* out = (__nv_bfloat16*)a.out0 + row * a.out0_stride;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      const int col = (c * 32 + lane) * 8;
+      if (col < cols) {
+        float h[8];
+        value(c, h);
+        if (OP == kModulate) {
+          f8 sc = unpack8(ld_cached(scale + col));
+          f8 sh = unpack8(ld_cached(shift + col));
+#pragma unroll
+          for (int j = 0; j < 8; ++j) h[j] = h[j] * (1.f + sc.v[j]) + sh.v[j];
+        }
+        st_stream(out + col, pack8(h));
+      }
+    }
+    return;
+  }
+
   float ss = 0.f;
 #pragma unroll
   for (int c = 0; c < NCH; ++c) {
     const int col = (c * 32 + lane) * 8;
     if (col < cols) {
-      f8 x0 = unpack8(raw0[c]);
-      if (kTwoIn) {
-        f8 x1 = unpack8(raw1[c]);
-        f8 g = unpack8(rawg[c]);
+      float h[8];
+      value(c, h);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) h[c][j] = x0.v[j] + g.v[j] * x1.v[j];
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) h[c][j] = x0.v[j];
-      }
-      if (kNorm) {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) ss += h[c][j] * h[c][j];
+      for (int j = 0; j < 8; ++j) ss += h[j] * h[j];
+      if (OP == kResRmsModulate) {
+        __nv_bfloat16* out0 = (__nv_bfloat16*)a.out0 + row * a.out0_stride;
+        st_stream(out0 + col, pack8(h));
       }
     }
   }
-
-  if (OP == kGatedResidual) {
-    __nv_bfloat16* out0 = (__nv_bfloat16*)a.out0 + row * a.out0_stride;
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      const int col = (c * 32 + lane) * 8;
-      if (col < cols) st_stream(out0 + col, pack8(h[c]));
-    }
-    return;
-  }
-  if (OP == kResRmsModulate) {
-    __nv_bfloat16* out0 = (__nv_bfloat16*)a.out0 + row * a.out0_stride;
-#pragma unroll
-    for (int c = 0; c < NCH; ++c) {
-      const int col = (c * 32 + lane) * 8;
-      if (col < cols) st_stream(out0 + col, pack8(h[c]));
-    }
-  }
-
-  float rstd = 1.f;
-  if (kNorm) {
-    ss = warp_sum(ss);
-    rstd = rsqrtf(ss / (float)cols + a.eps);
-  }
+  ss = warp_sum(ss);
+  const float rstd = rsqrtf(ss / (float)cols + a.eps);
   __nv_bfloat16* out =
       (__nv_bfloat16*)(OP == kResRmsModulate ? a.out1 : a.out0) +
       row * (OP == kResRmsModulate ? a.out1_stride : a.out0_stride);
@@ -126,17 +132,14 @@ __global__ void __launch_bounds__(kRowWarps * 32) adaln_rows_vec(RowArgs a) {
   for (int c = 0; c < NCH; ++c) {
     const int col = (c * 32 + lane) * 8;
     if (col < cols) {
+      float h[8];
+      value(c, h);
       f8 sc = unpack8(ld_cached(scale + col));
       f8 sh = unpack8(ld_cached(shift + col));
+      f8 w = unpack8(ld_cached(weight + col));
       float o[8];
-      if (kNorm) {
-        f8 w = unpack8(ld_cached(weight + col));
 #pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = (h[c][j] * rstd) * w.v[j] * (1.f + sc.v[j]) + sh.v[j];
-      } else {
-#pragma unroll
-        for (int j = 0; j < 8; ++j) o[j] = h[c][j] * (1.f + sc.v[j]) + sh.v[j];
-      }
+      for (int j = 0; j < 8; ++j) o[j] = (h[j] * rstd) * w.v[j] * (1.f + sc.v[j]) + sh.v[j];
       st_stream(out + col, pack8(o));
     }
   }
@@ -249,16 +252,31 @@ int launch_rows(const RowArgs& a, cudaStream_t s, const char* name) {
 
 // ---- SwiGLU and GELU-tanh -------------------------------------------------
 
-// x * sigmoid(x) with an IEEE division so tiny results stay accurate.
-__device__ __forceinline__ float silu(float g) { return g / (1.f + __expf(-g)); }
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcpf(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
-// gelu_tanh(x) = 0.5 x (1 + tanh(u)) = x * sigmoid(2u), u = sqrt(2/pi)(x + 0.044715 x^3).
-// The sigmoid form has no cancellation for negative x.
+// silu(g) = g * sigmoid(g) = g / (1 + 2^(-g log2 e)): two MUFU ops, relative
+// error a few fp32 ulps (results below 2^-126 flush to zero).
+__device__ __forceinline__ float silu(float g) {
+  return g * rcpf(1.f + ex2f(g * -1.4426950408889634f));
+}
+
+// gelu_tanh(x) = 0.5 x (1 + tanh(u)) = x * sigmoid(2u), u = sqrt(2/pi)(x + 0.044715 x^3),
+// i.e. x / (1 + 2^(x (c1 + c2 x^2))) with c1 = -2 sqrt(2/pi) log2(e), c2 = c1 * 0.044715.
+// The sigmoid form has no cancellation for negative x; two MUFU ops per element.
 __device__ __forceinline__ float gelu_tanh(float x) {
-  const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
-  const float k1 = 0.044715f;
-  const float u = k0 * (x + k1 * x * x * x);
-  return x / (1.f + __expf(-2.f * u));
+  const float c1 = -2.f * 0.7978845608028654f * 1.4426950408889634f;
+  const float c2 = c1 * 0.044715f;
+  const float e = ex2f(x * fmaf(c2, x * x, c1));
+  return x * rcpf(1.f + e);
 }
 
 constexpr int kEwThreads = 256;

@@ -190,6 +190,217 @@ __global__ void __launch_bounds__(256) qknorm_rope_pack_kernel(
   }
 }
 
+// ---- fast path: one warp per token, partner chunks owned by the same lane ------
+//
+// For head_dim D and rotary_dim rot with rot % 16 == 0 and (D - rot) % 16 == 0,
+// a head row is split into D/16 lane-owned chunk pairs of 8 columns: lane
+// l < rot/16 owns chunk l and its rotate-half partner chunk l + rot/16; the
+// remaining lanes own two consecutive pass-through chunks above rot. So the
+// rotation needs no cross-lane data, and the norm's sum of squares is a
+// (D/16)-lane shuffle reduction. One warp walks all heads of one token, so the
+// QK-norm weights and the token's cos/sin stay in registers across heads; v
+// head rows are a plain 16-byte copy.
+template <int D>
+struct PairLanes {
+  static constexpr int L = D / 16;  // lanes per head row
+  static constexpr int R = 32 / L;  // head rows per warp pass
+};
+
+template <int D>
+__device__ __forceinline__ void lane_chunks(int sub, int rot, int& c0, int& c1, bool& pair) {
+  const int np = rot / 16;
+  if (sub < np) {
+    c0 = sub;
+    c1 = sub + np;
+    pair = true;
+  } else {
+    c0 = rot / 8 + 2 * (sub - np);
+    c1 = c0 + 1;
+    pair = false;
+  }
+}
+
+// Normalise (fp32 sum over the head row) + rotate one head row's two chunks.
+template <int D>
+__device__ __forceinline__ void norm_rope_pair(const uint4& ra, const uint4& rb, const f8& w0,
+                                               const f8& w1, const float (&cs0)[8],
+                                               const float (&sn0)[8], const float (&cs1)[8],
+                                               const float (&sn1)[8], bool pair, float eps,
+                                               uint4& oa, uint4& ob) {
+  constexpr int L = PairLanes<D>::L;
+  f8 a = unpack8(ra), b = unpack8(rb);
+  float ss = 0.f;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) ss += a.v[j] * a.v[j] + b.v[j] * b.v[j];
+#pragma unroll
+  for (int o = L / 2; o > 0; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+  const float r = rsqrtf(ss / (float)D + eps);
+  float na[8], nb[8], xa[8], xb[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    na[j] = a.v[j] * r * w0.v[j];
+    nb[j] = b.v[j] * r * w1.v[j];
+  }
+  if (pair) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      xa[j] = na[j] * cs0[j] + (-nb[j]) * sn0[j];  // first half takes -partner
+      xb[j] = nb[j] * cs1[j] + na[j] * sn1[j];
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      xa[j] = na[j];
+      xb[j] = nb[j];
+    }
+  }
+  oa = pack8(xa);
+  ob = pack8(xb);
+}
+
+template <int D>
+__device__ __forceinline__ void load_rope_row(const float* cos_row, const float* sin_row, int c0,
+                                              int c1, bool pair, float (&cs0)[8], float (&sn0)[8],
+                                              float (&cs1)[8], float (&sn1)[8]) {
+#pragma unroll
+  for (int j = 0; j < 8; ++j) cs0[j] = sn0[j] = cs1[j] = sn1[j] = 0.f;
+  if (!pair) return;
+  const float4* c0p = reinterpret_cast<const float4*>(cos_row + 8 * c0);
+  const float4* s0p = reinterpret_cast<const float4*>(sin_row + 8 * c0);
+  const float4* c1p = reinterpret_cast<const float4*>(cos_row + 8 * c1);
+  const float4* s1p = reinterpret_cast<const float4*>(sin_row + 8 * c1);
+  float4 t;
+#define H3B_F8(dst, src)          \
+  t = __ldg(src);                 \
+  dst[0] = t.x, dst[1] = t.y, dst[2] = t.z, dst[3] = t.w; \
+  t = __ldg(src + 1);             \
+  dst[4] = t.x, dst[5] = t.y, dst[6] = t.z, dst[7] = t.w;
+  H3B_F8(cs0, c0p) H3B_F8(sn0, s0p) H3B_F8(cs1, c1p) H3B_F8(sn1, s1p)
+#undef H3B_F8
+}
+
+constexpr int kTokWarps = 8;  // tokens (warps) per CTA
+
+template <int D>
+__global__ void __launch_bounds__(kTokWarps * 32) qknorm_rope_pack_tok(
+    __nv_bfloat16* __restrict__ send, const __nv_bfloat16* __restrict__ q,
+    const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v, int64_t q_stride,
+    int64_t k_stride, int64_t v_stride, const __nv_bfloat16* __restrict__ wq,
+    const __nv_bfloat16* __restrict__ wk, const float* __restrict__ cos,
+    const float* __restrict__ sin, int64_t rows, int heads, int hl, int rot, float q_eps,
+    float k_eps) {
+  constexpr int L = PairLanes<D>::L;
+  constexpr int R = PairLanes<D>::R;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * kTokWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const int sub = lane % L, slot = lane / L;
+  int c0, c1;
+  bool pair;
+  lane_chunks<D>(sub, rot, c0, c1, pair);
+  const f8 wq0 = unpack8(ld_cached(wq + 8 * c0)), wq1 = unpack8(ld_cached(wq + 8 * c1));
+  const f8 wk0 = unpack8(ld_cached(wk + 8 * c0)), wk1 = unpack8(ld_cached(wk + 8 * c1));
+  float cs0[8], sn0[8], cs1[8], sn1[8];
+  load_rope_row<D>(cos + row * rot, sin + row * rot, c0, c1, pair, cs0, sn0, cs1, sn1);
+  const __nv_bfloat16* qr = q + row * q_stride;
+  const __nv_bfloat16* kr = k + row * k_stride;
+  const __nv_bfloat16* vr = v + row * v_stride;
+  auto dst_row = [&](int g, int part) {
+    const int dst = g / hl, lh = g - dst * hl;
+    return send + (((int64_t)dst * rows + row) * hl + lh) * (3 * D) + part * D;
+  };
+  // q and k head rows: 2H of them, R per pass, 2 passes in flight.
+  const int n_qk = 2 * heads;
+  for (int it = 0; it < n_qk; it += 2 * R) {
+    uint4 ra[2], rb[2];
+    int hr[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      hr[u] = it + u * R + slot;
+      const int h = hr[u] < n_qk ? hr[u] : n_qk - 1;  // idle lanes still join the shuffles
+      const __nv_bfloat16* src = (h < heads ? qr + h * D : kr + (h - heads) * D);
+      ra[u] = ld_stream(src + 8 * c0);
+      rb[u] = ld_stream(src + 8 * c1);
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      const bool is_k = (hr[u] < n_qk ? hr[u] : n_qk - 1) >= heads;
+      uint4 oa, ob;
+      norm_rope_pair<D>(ra[u], rb[u], is_k ? wk0 : wq0, is_k ? wk1 : wq1, cs0, sn0, cs1, sn1, pair,
+                        is_k ? k_eps : q_eps, oa, ob);
+      if (hr[u] < n_qk) {
+        const int g = is_k ? hr[u] - heads : hr[u];
+        __nv_bfloat16* o = dst_row(g, is_k ? 1 : 0);
+        st_stream(o + 8 * c0, oa);
+        st_stream(o + 8 * c1, ob);
+      }
+    }
+  }
+  // v head rows: copy, 16 bytes per lane, 4 copies in flight.
+  constexpr int C = D / 8;  // chunks per head row
+  const int n_v = heads * C;
+  for (int base = 0; base < n_v; base += 4 * 32) {
+    uint4 val[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int cidx = base + u * 32 + lane;
+      if (cidx < n_v) val[u] = ld_stream(vr + (int64_t)cidx * 8);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int cidx = base + u * 32 + lane;
+      if (cidx < n_v) {
+        const int g = cidx / C, cc = cidx - g * C;
+        st_stream(dst_row(g, 2) + 8 * cc, val[u]);
+      }
+    }
+  }
+}
+
+// Standalone fused_qknorm_rope on contiguous [B*S*H, D]: one warp per token
+// (B*S tokens, H heads each), cos/sin row = token % S.
+template <int D>
+__global__ void __launch_bounds__(kTokWarps * 32) qknorm_rope_tok(
+    __nv_bfloat16* __restrict__ out, const __nv_bfloat16* __restrict__ x,
+    const __nv_bfloat16* __restrict__ weight, const float* __restrict__ cos,
+    const float* __restrict__ sin, int64_t tokens, int heads, int64_t seq, int rot, float eps) {
+  constexpr int L = PairLanes<D>::L;
+  constexpr int R = PairLanes<D>::R;
+  const int lane = threadIdx.x & 31;
+  const int64_t tok = (int64_t)blockIdx.x * kTokWarps + (threadIdx.x >> 5);
+  if (tok >= tokens) return;
+  const int sub = lane % L, slot = lane / L;
+  int c0, c1;
+  bool pair;
+  lane_chunks<D>(sub, rot, c0, c1, pair);
+  const f8 w0 = unpack8(ld_cached(weight + 8 * c0)), w1 = unpack8(ld_cached(weight + 8 * c1));
+  float cs0[8], sn0[8], cs1[8], sn1[8];
+  const int64_t s_idx = tok % seq;
+  load_rope_row<D>(cos + s_idx * rot, sin + s_idx * rot, c0, c1, pair, cs0, sn0, cs1, sn1);
+  const __nv_bfloat16* xr = x + tok * heads * D;
+  __nv_bfloat16* orow = out + tok * heads * D;
+  for (int it = 0; it < heads; it += 2 * R) {
+    uint4 ra[2], rb[2];
+    int hr[2];
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      hr[u] = it + u * R + slot;
+      const int h = hr[u] < heads ? hr[u] : heads - 1;
+      ra[u] = ld_stream(xr + h * D + 8 * c0);
+      rb[u] = ld_stream(xr + h * D + 8 * c1);
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      uint4 oa, ob;
+      norm_rope_pair<D>(ra[u], rb[u], w0, w1, cs0, sn0, cs1, sn1, pair, eps, oa, ob);
+      if (hr[u] < heads) {
+        st_stream(orow + hr[u] * D + 8 * c0, oa);
+        st_stream(orow + hr[u] * D + 8 * c1, ob);
+      }
+    }
+  }
+}
+
 // ---- pack_qkv_destination_major (no arithmetic) ----------------------------
 
 template <int D>
@@ -301,6 +512,18 @@ extern "C" int h3b_qknorm_rope(void* out, const void* x, const void* weight, con
   auto* o = (__nv_bfloat16*)out;
   auto* xi = (const __nv_bfloat16*)x;
   auto* w = (const __nv_bfloat16*)weight;
+  if (shuffle && (head_dim - rotary_dim) % 16 == 0 && heads <= 0x7fffffff) {
+    const int64_t tokens = batch * seq;
+    const unsigned grid = (unsigned)((tokens + h3b::kTokWarps - 1) / h3b::kTokWarps);
+#define H3B_QT(DD)                                                                          \
+  if (head_dim == DD)                                                                       \
+    h3b::qknorm_rope_tok<DD><<<grid, h3b::kTokWarps * 32, 0, stream>>>(o, xi, w, cos, sin,    \
+                                                                      tokens, (int)heads,   \
+                                                                      seq, rot, eps);
+    H3B_QT(64) H3B_QT(128) H3B_QT(256)
+#undef H3B_QT
+    return h3b::check_launch("h3b_qknorm_rope");
+  }
 #define H3B_QK(DD)                                                                         \
   if (head_dim == DD) {                                                                    \
     if (shuffle)                                                                           \
@@ -341,6 +564,19 @@ extern "C" int h3b_qknorm_rope_pack(void* send, const void* q, const void* k, co
   const bool shuffle = rotary_dim % 16 == 0 && aligned16(cos) && aligned16(sin);
   const int hl = (int)(heads / world);
   auto* o = (__nv_bfloat16*)send;
+  if (shuffle && (head_dim - rotary_dim) % 16 == 0) {
+    const unsigned grid = (unsigned)((rows + h3b::kTokWarps - 1) / h3b::kTokWarps);
+#define H3B_QPT(DD)                                                                         \
+  if (head_dim == DD)                                                                       \
+    h3b::qknorm_rope_pack_tok<DD><<<grid, h3b::kTokWarps * 32, 0, stream>>>(                  \
+        o, (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,      \
+        q_row_stride, k_row_stride, v_row_stride, (const __nv_bfloat16*)q_weight,          \
+        (const __nv_bfloat16*)k_weight, cos, sin, rows, (int)heads, hl, (int)rotary_dim,   \
+        q_eps, k_eps);
+    H3B_QPT(64) H3B_QPT(128) H3B_QPT(256)
+#undef H3B_QPT
+    return h3b::check_launch("h3b_qknorm_rope_pack");
+  }
   const int64_t total_items = rows * 3 * heads;
 #define H3B_QKP(DD, SH)                                                                   \
   h3b::qknorm_rope_pack_kernel<DD, SH><<<(unsigned)((total_items + (256 / (DD / 8)) * h3b::kItems - 1) / \
