@@ -45,6 +45,7 @@ SIGNATURES: dict[str, list[Any]] = {
     "h3b_merge_heads": [_p, _p, _i64, _i64, _i64, _p],
     "h3b_attention": [_p, _p, _p, _p] + [_i64] * 17 + [_f32, _p, _i64, _p],
     "h3b_attention_workspace_size": [_i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_i64)],
+    "h3b_attention_noalloc": [_p, _p, _p, _p] + [_i64] * 17 + [_f32, _p],
     "h3b_clear_device_status": [_p],
 }
 

@@ -1002,3 +1002,88 @@ extern "C" int h3b_attention_workspace_size(int64_t batch, int64_t seq_q, int64_
   *bytes_out = make_plan(batch, seq_q, seq_k, heads).ws_bytes;
   return H3B_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point
+// ---------------------------------------------------------------------------
+//
+// Some callers cannot hand this library scratch memory. A host runtime that
+// reaches the kernels through the plain C ABI (an FFI binding inside a
+// serving process) often has no device allocator of its own: the device
+// memory belongs to another framework's pool, and calling cudaMalloc from the
+// hot loop would step around that pool and can synchronise the whole device.
+// h3b_attention_noalloc serves them: the split-tail workspace lives in the
+// fixed device array below, so the call allocates nothing.
+//
+// The array is kNoAllocScratchBytes (20 MiB) on every GPU that loads this
+// library, held until the process exits. It covers the largest split plan of a
+// B200 (148 SMs x 130 KiB per split CTA); a shape whose plan needs more is
+// rejected with H3B_ERR_VALUE. Every call on a device shares the one array and
+// finds whatever the previous call left there. Nothing in it has to start at
+// zero (each split CTA writes its whole slot before the combine kernel reads
+// it), but two calls whose kernels overlap on the GPU race on it: run them on
+// one stream, or order them.
+constexpr int64_t kNoAllocScratchBytes = 20ll << 20;
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[64] = {};
+
+// Device address of g_noalloc_scratch on the current device. The first call on
+// a device looks it up (cudaGetSymbolAddress, with that device current); in
+// host code the array's name is only a host-side stand-in and must never reach
+// a kernel.
+int noalloc_scratch(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 64) {
+    h3b::set_error("h3b_attention_noalloc: no usable current CUDA device");
+    return H3B_ERR_CUDA;
+  }
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      h3b::set_error(std::string("h3b_attention_noalloc: cannot resolve the scratch array: ") +
+                     cudaGetErrorString(e));
+      return H3B_ERR_CUDA;
+    }
+    g_noalloc_addr[dev] = p;
+  }
+  *out = g_noalloc_addr[dev];
+  return H3B_OK;
+}
+}  // namespace
+
+extern "C" int h3b_attention_noalloc(void* out, const void* q, const void* k, const void* v,
+                                     int64_t batch, int64_t seq_q, int64_t seq_k,
+                                     int64_t heads, int64_t head_dim, int64_t q_batch_stride,
+                                     int64_t q_row_stride, int64_t q_head_stride,
+                                     int64_t k_batch_stride, int64_t k_row_stride,
+                                     int64_t k_head_stride, int64_t v_batch_stride,
+                                     int64_t v_row_stride, int64_t v_head_stride,
+                                     int64_t o_batch_stride, int64_t o_row_stride,
+                                     int64_t o_head_stride, float softmax_scale,
+                                     h3b_stream_t stream) {
+  int64_t need = 0;
+  int rc = h3b_attention_workspace_size(batch, seq_q, seq_k, heads, head_dim, &need);
+  if (rc != H3B_OK) return rc;
+  if (need > kNoAllocScratchBytes) {
+    char buf[256];
+    snprintf(buf, sizeof(buf),
+             "h3b_attention_noalloc: this shape needs %lld bytes of split workspace, more than "
+             "the static maximum of %lld bytes; use h3b_attention with a caller workspace",
+             (long long)need, (long long)kNoAllocScratchBytes);
+    h3b::set_error(buf);
+    return H3B_ERR_VALUE;
+  }
+  void* scratch = nullptr;
+  if (need > 0 && (rc = noalloc_scratch(&scratch)) != H3B_OK) return rc;
+  return h3b_attention(out, q, k, v, batch, seq_q, seq_k, heads, head_dim, q_batch_stride,
+                       q_row_stride, q_head_stride, k_batch_stride, k_row_stride,
+                       k_head_stride, v_batch_stride, v_row_stride, v_head_stride,
+                       o_batch_stride, o_row_stride, o_head_stride, softmax_scale, scratch,
+                       need > 0 ? kNoAllocScratchBytes : 0, stream);
+}

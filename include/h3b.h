@@ -171,6 +171,26 @@ int h3b_attention(void* out, const void* q, const void* k, const void* v,
 int h3b_attention_workspace_size(int64_t batch, int64_t seq_q, int64_t seq_k, int64_t heads,
                                  int64_t head_dim, int64_t* bytes_out);
 
+/* h3b_attention for callers that cannot hand over scratch memory (no reference
+ * counterpart: the reference always runs in a framework that allocates). A
+ * caller that binds this library over a plain C FFI may own no device
+ * allocator, and cudaMalloc on its hot loop would bypass the process's memory
+ * pool and can synchronise the device. Here the split-tail workspace is a
+ * file-scope 20 MiB device array that every GPU loading the library keeps
+ * until exit; shapes needing more return H3B_ERR_VALUE. The first call on a
+ * device resolves the array's device address (cudaGetSymbolAddress): make that
+ * first call before any stream capture. All calls on a device share the
+ * array; calls whose kernels overlap on the GPU race, so keep them ordered.
+ * Nothing in this path calls cudaMalloc, cudaFree or an allocating library. */
+int h3b_attention_noalloc(void* out, const void* q, const void* k, const void* v,
+                          int64_t batch, int64_t seq_q, int64_t seq_k, int64_t heads,
+                          int64_t head_dim,
+                          int64_t q_batch_stride, int64_t q_row_stride, int64_t q_head_stride,
+                          int64_t k_batch_stride, int64_t k_row_stride, int64_t k_head_stride,
+                          int64_t v_batch_stride, int64_t v_row_stride, int64_t v_head_stride,
+                          int64_t o_batch_stride, int64_t o_row_stride, int64_t o_head_stride,
+                          float softmax_scale, h3b_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
