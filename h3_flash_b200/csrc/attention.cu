@@ -66,12 +66,12 @@ constexpr uint32_t kSmemQ = 0;
 constexpr uint32_t kSmemK = kSmemQ + kTiles * kTileBytes;
 constexpr uint32_t kSmemV = kSmemK + kKStages * kTileBytes;
 constexpr uint32_t kSmemBar = kSmemV + kVStages * kTileBytes;
-// barriers: q[2], kfull[3], kempty[3], vfull[2], vempty[2], s[2], p[2][2], o[2] + tmem slot + abort
-constexpr uint32_t kNumBars = kTiles + 2 * kKStages + 2 * kVStages + 4 * kTiles;
-// Row-max / row-sum exchange between the two warps that share a TMEM lane
-// quadrant: float [tile][parity][key half][128 rows].
+// barriers: q[2], kfull, kempty, vfull, vempty, s[2], p[2][2], o[2], x[2][4] + tmem slot + abort
+constexpr uint32_t kNumBars = kTiles + 2 * kKStages + 2 * kVStages + 4 * kTiles + 4 * kTiles;
+// Row-max / row-sum exchange between the four warps that share a TMEM lane
+// quadrant: float [tile][parity][key segment 4][128 rows].
 constexpr uint32_t kSmemXch = kSmemBar + ((kNumBars * 8 + 16 + 127) / 128) * 128;
-constexpr uint32_t kSmemBytes = kSmemXch + kTiles * 2 * 2 * kBlockM * 4;
+constexpr uint32_t kSmemBytes = kSmemXch + kTiles * 2 * 4 * kBlockM * 4;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;  // slack to 1024-align the base
 
 constexpr uint32_t kTmemCols = 512;
@@ -303,6 +303,15 @@ __device__ __forceinline__ void tmem_ld_wait16(uint32_t (&r)[16]) {
                  "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]));
 }
 
+__device__ __forceinline__ void tmem_pin16(uint32_t (&r)[16]) {
+  asm volatile(""
+               : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
+                 "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
+                 "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]));
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]);
+
 __device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t (&r)[8]) {
   asm volatile(
       "tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"r"(taddr),
@@ -416,6 +425,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto bar_o = [&](int t) {
     return bars + 8u * (kTiles + 2 * kKStages + 2 * kVStages + 3 * kTiles + t);
   };
+  // bar_x(t, quad): the four softmax warps of a lane quadrant have published their
+  // partial row maxima of tile t for this block.
+  auto bar_x = [&](int t, int quad) {
+    return bars + 8u * (kTiles + 2 * kKStages + 2 * kVStages + 4 * kTiles + 4 * t + quad);
+  };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemBar + kNumBars * 8);
   volatile uint32_t* abort_flag = tmem_slot + 1;
 
@@ -440,9 +454,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < kTiles; ++t) {
       mbar_init(bar_q(t), 1);
       mbar_init(bar_s(t), 1);
-      mbar_init(bar_p(t, 0), 128);
-      mbar_init(bar_p(t, 1), 128);
+      mbar_init(bar_p(t, 0), 256);
+      mbar_init(bar_p(t, 1), 256);
       mbar_init(bar_o(t), 1);
+      for (int qd = 0; qd < 4; ++qd) mbar_init(bar_x(t, qd), 128);
     }
     for (int s = 0; s < kKStages; ++s) {
       mbar_init(bar_kfull(s), 1);
@@ -532,12 +547,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto issue_pv = [&](int t, int j, int h) {
         const uint64_t vd = v_desc0 + (uint64_t)(((j % kVStages) * kTileBytes) >> 4);
         const uint32_t d = tmem + kTmemO + t * 128;
-        const uint32_t a = tmem + kTmemS + t * 128 + h * 64;
 #pragma unroll
         for (int k4 = 0; k4 < kBlockN / 32; ++k4) {
           const int kk = h * (kBlockN / 32) + k4;
-          mma_ts(d, a + k4 * 8, vd + (uint64_t)((kk * 2048) >> 4), idesc_pv,
-                 (j > 0 || kk > 0) ? 1u : 0u);
+          // keys 16kk..16kk+15 = segment kk/2, second 16 of it if kk is odd
+          mma_ts(d, tmem + kTmemS + t * 128 + (kk >> 1) * 32 + (kk & 1) * 8,
+                 vd + (uint64_t)((kk * 2048) >> 4), idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         }
       };
       if (ok) ok = wait_bar(bar_kfull(0), 0, abort_flag, prm.status);
@@ -581,170 +596,168 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- softmax: 8 warps per query tile ----------------
-    const int t = warp >> 3;         // query tile
-    const int quad = warp & 3;       // TMEM lane quadrant: rows 32*quad .. +31
-    const int hk = (warp >> 2) & 1;  // key half [64hk, 64hk+64) of every block
+    // ---------------- softmax: all 16 warps on whichever tile is ready ----------------
+    // Warp w owns TMEM lane quadrant w%4 (query rows 32(w%4)..+31) and key segment
+    // w/4 (block keys [32 seg, 32 seg + 32)) of BOTH tiles; per block it first does
+    // tile 0, then tile 1, so while the MMA warp works on one tile every softmax
+    // warp works on the other (four warps per SMSP share the latency hiding).
+    const int quad = warp & 3;
+    const int seg = warp >> 2;
+    const int hk = seg >> 1;  // key half whose P barrier this warp arrives on
     const int row_in_tile = quad * 32 + lane;
     const uint32_t lanes = (uint32_t)(quad * 32) << 16;
-    const uint32_t t_s = tmem + lanes + kTmemS + t * 128 + hk * 64;  // this warp's S columns
-    const uint32_t t_o = tmem + lanes + kTmemO + t * 128 + hk * 64;  // this warp's O columns
     float* xch = reinterpret_cast<float*>(smem + kSmemXch);
-    auto xslot = [&](int parity, int half) {
-      return xch + ((t * 2 + parity) * 2 + half) * kBlockM + row_in_tile;
+    auto xslot = [&](int t, int parity, int sg) {
+      return xch + ((t * 2 + parity) * 4 + sg) * kBlockM + row_in_tile;
     };
-    const uint32_t pair_bar = 1 + t * 4 + quad;  // named barrier of the two warps on these rows
+    const uint32_t quad_bar = 1 + quad;  // named barrier of the four warps on these rows
     const float c = prm.scale_log2;
-    float m_use = -INFINITY;
-    float l_sum = 0.f;
+    float m_use[kTiles] = {-INFINITY, -INFINITY};
+    float l_sum[kTiles] = {0.f, 0.f};
     bool ok = true;
-    for (int j = 0; j < n_kv; ++j) {
-      ok = wait_bar(bar_s(t), j & 1, abort_flag, prm.status);
-      // tcgen05.ld/st below are warp-collective; the named barrier is pair-collective.
+    for (int j = 0; j < n_kv && ok; ++j) {
+#pragma unroll
+      for (int t = 0; t < kTiles; ++t) {
+        const uint32_t t_s = tmem + lanes + kTmemS + t * 128 + seg * 32;  // this warp's S columns
+        const uint32_t t_o = tmem + lanes + kTmemO + t * 128 + seg * 32;  // and O columns
+        ok = wait_bar(bar_s(t), j & 1, abort_flag, prm.status);
+        // tcgen05.ld/st below are warp-collective; the named barrier is quad-collective.
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+        const int valid = prm.seq_k - (j0 + j) * kBlockN - seg * 32;  // keys of this segment
+        // One TMEM pass: the warp's 32 columns of S, in two 16-column loads.
+        uint32_t sv[2][16];
+        tmem_ld16(t_s, sv[0]);
+        tmem_ld16(t_s + 16, sv[1]);
+        tmem_ld_wait16(sv[0]);
+        tmem_pin16(sv[1]);
+        if (valid < 32) {
+          mask_keys16(sv[0], 0, valid);
+          mask_keys16(sv[1], 16, valid);
+        }
+        float mxp[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          mxp[i] = max3(__uint_as_float(sv[0][4 * i]), __uint_as_float(sv[0][4 * i + 1]),
+                        __uint_as_float(sv[0][4 * i + 2]));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          mxp[i] = max3(mxp[i], __uint_as_float(sv[0][4 * i + 3]), __uint_as_float(sv[1][4 * i]));
+          mxp[i] = max3(mxp[i], __uint_as_float(sv[1][4 * i + 1]),
+                        __uint_as_float(sv[1][4 * i + 2]));
+          mxp[i] = fmaxf(mxp[i], __uint_as_float(sv[1][4 * i + 3]));
+        }
+        // Publish this warp's partial max (non-blocking), then exponentiate
+        // against the running max while the quadrant's other warps catch up.
+        *xslot(t, j & 1, seg) = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
+        mbar_arrive(bar_x(t, quad));
+        // p = 2^(s*c - m) for the 16 column pairs, packed fp32x2; kPolyPairs of
+        // every 8 pairs use the FMA-pipe exp2 so MUFU and FMA share the work.
+        float2 lp[2];
+        uint32_t pk[16];
+        auto exponentiate = [&](float m) {
+          const float2 c2 = make_float2(c, c);
+          const float2 nm2 = make_float2(-m, -m);
+          lp[0] = lp[1] = make_float2(0.f, 0.f);
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const uint32_t* src = sv[i >> 3];
+            const int k = (i & 7) * 2;
+            const float2 x = __ffma2_rn(
+                make_float2(__uint_as_float(src[k]), __uint_as_float(src[k + 1])), c2, nm2);
+            float2 p;
+            if ((i & 7) >= 8 - kPolyPairs) {
+              p = exp2_poly(x);
+            } else {
+              p.x = ex2(x.x);
+              p.y = ex2(x.y);
+            }
+            lp[i & 1] = __fadd2_rn(lp[i & 1], p);
+            pk[i] = pack_bf16(p.x, p.y);
+          }
+        };
+        if (j > 0) exponentiate(m_use[t]);
+        ok = wait_bar(bar_x(t, quad), j & 1, abort_flag, prm.status);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        const float mx = fmaxf(fmaxf(*xslot(t, j & 1, 0), *xslot(t, j & 1, 1)),
+                               fmaxf(*xslot(t, j & 1, 2), *xslot(t, j & 1, 3)));
+        const float m_new = mx * c;
+        const bool need = m_new > m_use[t] + kRescaleThreshold;  // same in the 4 warps
+        if (__any_sync(0xffffffffu, need)) {
+          if (j > 0) {
+            // PV_t(j-1) is complete: the S_t(j) commit covers every earlier MMA.
+            const float alpha = need ? ex2(m_use[t] - m_new) : 1.f;
+            uint32_t o[32];
+            tmem_ld32(t_o, o);
+            tmem_ld_wait(o);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(t_o, o);
+            l_sum[t] *= alpha;
+          }
+          if (need) m_use[t] = m_new;
+          exponentiate(m_use[t]);  // redo against the new running max
+        }
+        // P (bf16) of the 32 keys goes to S columns [32 seg, 32 seg + 16), already read.
+        tmem_st16(t_s, pk);
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(bar_p(t, hk));
+        l_sum[t] += (lp[0].x + lp[0].y) + (lp[1].x + lp[1].y);
+      }
+    }
+    // ---------------- epilogue: O / l -> bf16 (or fp32 partials) ----------------
+#pragma unroll
+    for (int t = 0; t < kTiles; ++t) {
+      if (!ok) break;
+      const uint32_t t_o = tmem + lanes + kTmemO + t * 128 + seg * 32;
+      ok = wait_bar(bar_o(t), 0, abort_flag, prm.status);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const int valid = prm.seq_k - (j0 + j) * kBlockN - hk * 64;  // keys of this half that exist
-      // Pass 1: max over this warp's 64 columns, then combine with the partner.
-      float mx;
-      {
-        uint32_t a[32], b[32];
-        tmem_ld32(t_s, a);
-        tmem_ld32(t_s + 32, b);
-        tmem_ld_wait(a);
-        tmem_pin(b);
-        if (valid < 64) {
-          mask_keys(a, 0, valid);
-          mask_keys(b, 32, valid);
-        }
-        float mxp[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          mxp[i] = max3(__uint_as_float(a[4 * i]), __uint_as_float(a[4 * i + 1]),
-                        __uint_as_float(a[4 * i + 2]));
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          mxp[i] = max3(mxp[i], __uint_as_float(a[4 * i + 3]), __uint_as_float(b[4 * i]));
-          mxp[i] = max3(mxp[i], __uint_as_float(b[4 * i + 1]), __uint_as_float(b[4 * i + 2]));
-          mxp[i] = fmaxf(mxp[i], __uint_as_float(b[4 * i + 3]));
-        }
-        mx = fmaxf(fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3])),
-                   fmaxf(fmaxf(mxp[4], mxp[5]), fmaxf(mxp[6], mxp[7])));
-      }
-      *xslot(j & 1, hk) = mx;
-      named_bar_sync(pair_bar, 64);
-      mx = fmaxf(mx, *xslot(j & 1, hk ^ 1));
-      const float m_new = mx * c;
-      const bool need = m_new > m_use + kRescaleThreshold;  // same in both warps of the pair
-      // tcgen05.ld/st are warp-collective: the whole warp rescales if any row must.
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // PV_t(j-1) is complete: the S_t(j) commit covers every earlier MMA.
-        const float alpha = need ? ex2(m_use - m_new) : 1.f;
-#pragma unroll 1
-        for (int q2 = 0; q2 < 2; ++q2) {
-          uint32_t o[32];
-          tmem_ld32(t_o + q2 * 32, o);
-          tmem_ld_wait(o);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(t_o + q2 * 32, o);
-        }
-        l_sum *= alpha;
-      }
-      if (need) m_use = m_new;
-      // Pass 2: p = 2^(s*c - m) in 16-column chunks, the next chunk's tcgen05.ld
-      // in flight while this one is exponentiated. Column pairs run in packed
-      // fp32x2; kPolyPairs of every 8 pairs use the FMA-pipe exp2 so the MUFU
-      // and FMA pipes share the exponentials. P (bf16) of chunk q goes to S
-      // columns [8q, 8q+8) of this warp's range, which pass 2 has already read.
-      const float2 c2 = make_float2(c, c);
-      const float2 nm2 = make_float2(-m_use, -m_use);
-      float2 lp[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-      uint32_t sb[2][16];
-      tmem_ld16(t_s, sb[0]);
-      tmem_ld_wait16(sb[0]);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint32_t(&cur)[16] = sb[q & 1];
-        if (q < 3) tmem_ld16(t_s + (q + 1) * 16, sb[(q + 1) & 1]);
-        if (valid < 64) mask_keys16(cur, q * 16, valid);
-        uint32_t pk[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          const float2 x = __ffma2_rn(
-              make_float2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1])), c2, nm2);
-          float2 p;
-          if (((q * 8 + i) & 7) >= 8 - kPolyPairs) {
-            p = exp2_poly(x);
-          } else {
-            p.x = ex2(x.x);
-            p.y = ex2(x.y);
-          }
-          lp[i & 1] = __fadd2_rn(lp[i & 1], p);
-          pk[i] = pack_bf16(p.x, p.y);
-        }
-        tmem_st8(t_s + q * 8, pk);
-        if (q < 3) tmem_ld_wait16(sb[(q + 1) & 1]);
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(bar_p(t, hk));
-      l_sum += (lp[0].x + lp[0].y) + (lp[1].x + lp[1].y);
-    }
-    // ---------------- epilogue: O / l -> bf16 -> global ----------------
-    if (ok) ok = wait_bar(bar_o(t), 0, abort_flag, prm.status);
-    ok = __all_sync(0xffffffffu, ok);
-    if (ok) {
-      tc_fence_after();
-      // Row sum = both halves' shares (the parity after the last max exchange).
-      *xslot(n_kv & 1, hk) = l_sum;
-      named_bar_sync(pair_bar, 64);
-      const float l_row = l_sum + *xslot(n_kv & 1, hk ^ 1);
+      // Row sum = the four segments' shares (parity slot after the last exchange).
+      *xslot(t, n_kv & 1, seg) = l_sum[t];
+      named_bar_sync(quad_bar, 128);
+      const float l_row = (*xslot(t, n_kv & 1, 0) + *xslot(t, n_kv & 1, 1)) +
+                          (*xslot(t, n_kv & 1, 2) + *xslot(t, n_kv & 1, 3));
+      uint32_t o[32];
+      tmem_ld32(t_o, o);
+      tmem_ld_wait(o);
       if (split_slot >= 0) {
         // Partial result of a key range: unnormalised O and (running max, sum).
         float* ws = prm.ws + (int64_t)split_slot * kWsSlotFloats + t * kWsTileFloats;
-        float* o_row = ws + row_in_tile * kHeadDim + hk * 64;
-#pragma unroll 1
-        for (int q2 = 0; q2 < 2; ++q2) {
-          uint32_t o[32];
-          tmem_ld32(t_o + q2 * 32, o);
-          tmem_ld_wait(o);
+        float* o_row = ws + row_in_tile * kHeadDim + seg * 32;
 #pragma unroll
-          for (int v4 = 0; v4 < 8; ++v4)
-            *reinterpret_cast<float4*>(o_row + q2 * 32 + v4 * 4) =
-                make_float4(__uint_as_float(o[v4 * 4 + 0]), __uint_as_float(o[v4 * 4 + 1]),
-                            __uint_as_float(o[v4 * 4 + 2]), __uint_as_float(o[v4 * 4 + 3]));
-        }
-        if (hk == 0) {
+        for (int v4 = 0; v4 < 8; ++v4)
+          *reinterpret_cast<float4*>(o_row + v4 * 4) =
+              make_float4(__uint_as_float(o[v4 * 4 + 0]), __uint_as_float(o[v4 * 4 + 1]),
+                          __uint_as_float(o[v4 * 4 + 2]), __uint_as_float(o[v4 * 4 + 3]));
+        if (seg == 0) {
           float* ml = ws + kBlockM * kHeadDim + 2 * row_in_tile;
-          ml[0] = m_use;
+          ml[0] = m_use[t];
           ml[1] = l_row;
         }
       } else {
         const float inv_l = 1.f / l_row;
         const int row = q_row0 + t * kBlockM + row_in_tile;
-        __nv_bfloat16* dst = prm.out + (int64_t)batch * prm.o_batch_stride +
-                             (int64_t)row * prm.o_row_stride +
-                             (int64_t)head * prm.o_head_stride + hk * 64;
-#pragma unroll 1
-        for (int q2 = 0; q2 < 2; ++q2) {
-          uint32_t o[32];
-          tmem_ld32(t_o + q2 * 32, o);
-          tmem_ld_wait(o);
-          if (row < prm.seq_q) {
+        if (row < prm.seq_q) {
+          __nv_bfloat16* dst = prm.out + (int64_t)batch * prm.o_batch_stride +
+                               (int64_t)row * prm.o_row_stride +
+                               (int64_t)head * prm.o_head_stride + seg * 32;
 #pragma unroll
-            for (int v8 = 0; v8 < 4; ++v8) {
-              uint4 u;
-              u.x = pack_bf16(__uint_as_float(o[v8 * 8 + 0]) * inv_l,
-                              __uint_as_float(o[v8 * 8 + 1]) * inv_l);
-              u.y = pack_bf16(__uint_as_float(o[v8 * 8 + 2]) * inv_l,
-                              __uint_as_float(o[v8 * 8 + 3]) * inv_l);
-              u.z = pack_bf16(__uint_as_float(o[v8 * 8 + 4]) * inv_l,
-                              __uint_as_float(o[v8 * 8 + 5]) * inv_l);
-              u.w = pack_bf16(__uint_as_float(o[v8 * 8 + 6]) * inv_l,
-                              __uint_as_float(o[v8 * 8 + 7]) * inv_l);
-              *reinterpret_cast<uint4*>(dst + q2 * 32 + v8 * 8) = u;
-            }
+          for (int v8 = 0; v8 < 4; ++v8) {
+            uint4 u;
+            u.x = pack_bf16(__uint_as_float(o[v8 * 8 + 0]) * inv_l,
+                            __uint_as_float(o[v8 * 8 + 1]) * inv_l);
+            u.y = pack_bf16(__uint_as_float(o[v8 * 8 + 2]) * inv_l,
+                            __uint_as_float(o[v8 * 8 + 3]) * inv_l);
+            u.z = pack_bf16(__uint_as_float(o[v8 * 8 + 4]) * inv_l,
+                            __uint_as_float(o[v8 * 8 + 5]) * inv_l);
+            u.w = pack_bf16(__uint_as_float(o[v8 * 8 + 6]) * inv_l,
+                            __uint_as_float(o[v8 * 8 + 7]) * inv_l);
+            *reinterpret_cast<uint4*>(dst + v8 * 8) = u;
           }
         }
       }
