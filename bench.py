@@ -38,6 +38,7 @@ import torch
 
 ROOT = Path(__file__).resolve().parent
 METRIC = "DiT block fwd ms at S=49,920 (480p-5s) on 1/2/4/8 B200; a2a GB/s vs NVLink"
+NVLINK_PEER_GBS = 770.0  # measured peer copy, GB/s per direction per GPU
 L2_FLUSH_BYTES = 256 << 20
 
 
@@ -273,7 +274,7 @@ def run_h3b(args) -> dict | None:
     if world > 1:
         from h3_flash_b200.runtime.parallel import install_packed_ulysses
 
-        runtime = install_packed_ulysses(stack)
+        runtime = install_packed_ulysses(stack, exchange=args.exchange)
         runtime.begin_request()
     start, stop = split_bounds(cfg.seq, world, rank)
     rows = stop - start
@@ -364,6 +365,10 @@ def run_h3b(args) -> dict | None:
     ew_ms = _max_over_ranks(ew_ms, world)
     a2a_bytes = (4 * r * d * 2) * (world - 1) / world if world > 1 else 0.0
     a2a_ms = _max_over_ranks(sum(sections.get("all_to_all", [0.0])) / max(args.steps, 1), world)
+    if world > 1 and args.exchange == "p2p":
+        # the QKV exchange happens inside the pack kernel: count the whole pack
+        a2a_ms = _max_over_ranks(sum(sections.get("all_to_all", [0.0]) + sections.get("qknorm_rope_pack", [0.0]))
+                                 / max(args.steps, 1), world)
     sections_total = {k: round(sum(v) / args.steps, 4) for k, v in sections.items()}
 
     if rank != 0:
@@ -386,7 +391,8 @@ def run_h3b(args) -> dict | None:
             "seq": cfg.seq, "video_tokens": cfg.video_tokens, "audio_tokens": cfg.audio_tokens,
             "dim": cfg.dim, "heads": cfg.heads, "head_dim": cfg.head_dim, "ffn": f"{cfg.ffn_inner} gelu-tanh",
             "rotary_dim": cfg.rotary_dim, "rows_per_rank": rows, "heads_per_rank": hl,
-            "parallelism": f"ulysses_sp{world}", "l2": "flushed between timed steps (256 MiB write, then read back)",
+            "parallelism": f"ulysses_sp{world}",
+            "exchange": (args.exchange if world > 1 else "none"), "l2": "flushed between timed steps (256 MiB write, then read back)",
         },
         "e2e": {"value": round(e2e_mean, 4), "unit": "ms",
                 "h2d_bytes_per_step": hidden_host.numel() * hidden_host.element_size(),
@@ -413,8 +419,10 @@ def run_h3b(args) -> dict | None:
                                 if ew_ms else None},
             "all_to_all_nvlink": {"bytes_sent_per_gpu": a2a_bytes, "ms": round(a2a_ms, 4),
                                   "achieved_gbs": round(a2a_bytes / (a2a_ms * 1e-3) / 1e9, 1) if a2a_ms else None,
-                                  "nominal_gbs": 900.0,
-                                  "frac": round(a2a_bytes / (a2a_ms * 1e-3) / 1e9 / 900.0, 4) if a2a_ms else None},
+                                  "peak_gbs": NVLINK_PEER_GBS, "nominal_gbs": 900.0,
+                                  "peak_note": "measured peer copy per direction on this pool",
+                                  "frac": round(a2a_bytes / (a2a_ms * 1e-3) / 1e9 / NVLINK_PEER_GBS, 4)
+                                  if a2a_ms else None},
         },
         "sections_ms_per_step": sections_total,
         "gpu_launches": launches,
@@ -533,6 +541,8 @@ def main() -> int:
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["h3b", "reference"], default="h3b")
     parser.add_argument("--config", default="480p-5s")
+    parser.add_argument("--exchange", choices=["nccl", "p2p"], default="nccl",
+                        help="packed-Ulysses row exchange for N>1: NCCL all-to-all or NVLink peer stores")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--sweep", choices=["elementwise"], help="print the config-2 kernel sweep instead")
     parser.add_argument("--profile-kernel", choices=["attention", "elementwise"],

@@ -8,6 +8,7 @@ travels with the source tree needs nothing but the NVIDIA driver at run time.
 from __future__ import annotations
 
 import concurrent.futures
+import fcntl
 import os
 import shutil
 import subprocess
@@ -76,9 +77,19 @@ def build(force: bool = False, verbose: bool = False, ptxas_verbose: bool = Fals
 
     if not force and not is_stale():
         return LIB_PATH
+    LIB_DIR.mkdir(parents=True, exist_ok=True)
+    # Processes started together (one per GPU) build once: the others wait on
+    # the lock and then find the library fresh.
+    with open(LIB_DIR / ".build.lock", "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        if not force and not is_stale():
+            return LIB_PATH
+        return _build_locked(verbose, ptxas_verbose)
+
+
+def _build_locked(verbose: bool, ptxas_verbose: bool) -> Path:
     nvcc = nvcc_path()
     OBJ_DIR.mkdir(parents=True, exist_ok=True)
-    LIB_DIR.mkdir(parents=True, exist_ok=True)
     extra = ["-Xptxas", "-v"] if ptxas_verbose else []
     sources = _sources()
     with concurrent.futures.ThreadPoolExecutor(max_workers=min(8, len(sources))) as pool:

@@ -21,7 +21,8 @@ H3B_OK = 0
 H3B_ERR_VALUE = 1
 H3B_ERR_CUDA = 2
 H3B_ERR_UNSUPPORTED = 3
-ABI_VERSION = 2
+ABI_VERSION = 3
+IPC_HANDLE_BYTES = 64
 
 _p = ctypes.c_void_p
 _i64 = ctypes.c_int64
@@ -47,6 +48,13 @@ SIGNATURES: dict[str, list[Any]] = {
     "h3b_attention_workspace_size": [_i64, _i64, _i64, _i64, _i64, ctypes.POINTER(_i64)],
     "h3b_attention_noalloc": [_p, _p, _p, _p] + [_i64] * 17 + [_f32, _p],
     "h3b_clear_device_status": [_p],
+    "h3b_qknorm_rope_pack_p2p": [_p, _i64, _i64, _i64, _p, _p, _p, _i64, _i64, _i64, _p, _p, _p,
+                                 _p, _i64, _i64, _i64, _i64, _f32, _f32, _p],
+    "h3b_scatter_heads_p2p": [_p, _p, _p, _i64, _i64, _i64, _i64, _p],
+    "h3b_peer_barrier": [_p, _i64, _i64, _p],
+    "h3b_ipc_handle": [_p, _p, ctypes.POINTER(_i64)],
+    "h3b_ipc_open": [_p, _i64, ctypes.POINTER(_p)],
+    "h3b_ipc_close": [_p, _i64],
 }
 
 
@@ -84,6 +92,8 @@ def load() -> ctypes.CDLL:
         lib.h3b_last_error.restype = ctypes.c_char_p
         lib.h3b_device_status.argtypes = [ctypes.POINTER(ctypes.c_int)]
         lib.h3b_device_status.restype = ctypes.c_int
+        lib.h3b_peer_flags_bytes.argtypes = []
+        lib.h3b_peer_flags_bytes.restype = ctypes.c_int64
         version = lib.h3b_abi_version()
         if version != ABI_VERSION:
             raise RuntimeError(f"libh3b.so ABI {version} != expected {ABI_VERSION}")
@@ -92,7 +102,8 @@ def load() -> ctypes.CDLL:
 
 
 def exported_symbols() -> list[str]:
-    return sorted(SIGNATURES) + ["h3b_abi_version", "h3b_last_error", "h3b_device_status"]
+    return sorted(SIGNATURES) + ["h3b_abi_version", "h3b_last_error", "h3b_device_status",
+                                 "h3b_peer_flags_bytes"]
 
 
 def check(code: int, what: str) -> None:
@@ -107,7 +118,8 @@ def check(code: int, what: str) -> None:
 
 
 _LAUNCHES = 0
-_NON_KERNEL = {"h3b_clear_device_status", "h3b_attention_workspace_size"}
+_NON_KERNEL = {"h3b_clear_device_status", "h3b_attention_workspace_size", "h3b_ipc_handle",
+               "h3b_ipc_open", "h3b_ipc_close"}
 
 
 def call(name: str, *args: Any) -> None:

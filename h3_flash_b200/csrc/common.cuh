@@ -49,6 +49,21 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return r;
 }
 
+// Device pointers of one buffer on every rank of a peer-mapped group (this
+// rank's own entry is its local pointer). Passed by value as a kernel argument.
+constexpr int kMaxPeers = 16;
+struct PeerPtrs {
+  void* p[kMaxPeers];
+};
+// p[i] for a runtime i without spilling the parameter array to local memory.
+__device__ __forceinline__ void* peer_at(const PeerPtrs& pp, int i) {
+  void* r = pp.p[0];
+#pragma unroll
+  for (int j = 1; j < kMaxPeers; ++j)
+    if (i == j) r = pp.p[j];
+  return r;
+}
+
 struct f8 {
   float v[8];
 };

@@ -281,14 +281,48 @@ __device__ __forceinline__ void load_rope_row(const float* cos_row, const float*
 
 constexpr int kTokWarps = 8;  // tokens (warps) per CTA
 
-template <int D>
+// Where the packed head rows go. LocalSend is the destination-major send buffer
+// [W, rows, hl, 3D] that an all-to-all then exchanges; PeerRecv is every rank's
+// receive buffer [S_total, hl, 3D] (this rank's own included), mapped into this
+// process over NVLink, so the store itself is the exchange: row `row` of this
+// rank lands at global row row_offset + row of the owner of its head.
+struct LocalSend {
+  __nv_bfloat16* send;
+  int64_t rows;
+  int hl;
+  template <int D>
+  __device__ __forceinline__ __nv_bfloat16* at(int64_t row, int g, int part) const {
+    const int dst = g / hl, lh = g - dst * hl;
+    return send + (((int64_t)dst * rows + row) * hl + lh) * (3 * D) + part * D;
+  }
+  __device__ __forceinline__ void store(void* p, uint4 v) const { st_stream(p, v); }
+  __device__ __forceinline__ void finish() const {}
+};
+
+struct PeerRecv {
+  PeerPtrs recv;
+  int64_t row_offset;
+  int hl;
+  template <int D>
+  __device__ __forceinline__ __nv_bfloat16* at(int64_t row, int g, int part) const {
+    const int dst = g / hl, lh = g - dst * hl;
+    return reinterpret_cast<__nv_bfloat16*>(peer_at(recv, dst)) +
+           ((row_offset + row) * hl + lh) * (3 * D) + part * D;
+  }
+  __device__ __forceinline__ void store(void* p, uint4 v) const {
+    *reinterpret_cast<uint4*>(p) = v;
+  }
+  // Peers read these rows after a cross-rank barrier; order the stores first.
+  __device__ __forceinline__ void finish() const { __threadfence_system(); }
+};
+
+template <int D, class Dst>
 __global__ void __launch_bounds__(kTokWarps * 32) qknorm_rope_pack_tok(
-    __nv_bfloat16* __restrict__ send, const __nv_bfloat16* __restrict__ q,
-    const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v, int64_t q_stride,
-    int64_t k_stride, int64_t v_stride, const __nv_bfloat16* __restrict__ wq,
-    const __nv_bfloat16* __restrict__ wk, const float* __restrict__ cos,
-    const float* __restrict__ sin, int64_t rows, int heads, int hl, int rot, float q_eps,
-    float k_eps) {
+    Dst out, const __nv_bfloat16* __restrict__ q, const __nv_bfloat16* __restrict__ k,
+    const __nv_bfloat16* __restrict__ v, int64_t q_stride, int64_t k_stride, int64_t v_stride,
+    const __nv_bfloat16* __restrict__ wq, const __nv_bfloat16* __restrict__ wk,
+    const float* __restrict__ cos, const float* __restrict__ sin, int64_t rows, int heads,
+    int rot, float q_eps, float k_eps) {
   constexpr int L = PairLanes<D>::L;
   constexpr int R = PairLanes<D>::R;
   const int lane = threadIdx.x & 31;
@@ -305,10 +339,7 @@ __global__ void __launch_bounds__(kTokWarps * 32) qknorm_rope_pack_tok(
   const __nv_bfloat16* qr = q + row * q_stride;
   const __nv_bfloat16* kr = k + row * k_stride;
   const __nv_bfloat16* vr = v + row * v_stride;
-  auto dst_row = [&](int g, int part) {
-    const int dst = g / hl, lh = g - dst * hl;
-    return send + (((int64_t)dst * rows + row) * hl + lh) * (3 * D) + part * D;
-  };
+  auto dst_row = [&](int g, int part) { return out.template at<D>(row, g, part); };
   // q and k head rows: 2H of them, R per pass, 2 passes in flight.
   const int n_qk = 2 * heads;
   for (int it = 0; it < n_qk; it += 2 * R) {
@@ -331,8 +362,8 @@ __global__ void __launch_bounds__(kTokWarps * 32) qknorm_rope_pack_tok(
       if (hr[u] < n_qk) {
         const int g = is_k ? hr[u] - heads : hr[u];
         __nv_bfloat16* o = dst_row(g, is_k ? 1 : 0);
-        st_stream(o + 8 * c0, oa);
-        st_stream(o + 8 * c1, ob);
+        out.store(o + 8 * c0, oa);
+        out.store(o + 8 * c1, ob);
       }
     }
   }
@@ -351,10 +382,11 @@ __global__ void __launch_bounds__(kTokWarps * 32) qknorm_rope_pack_tok(
       const int cidx = base + u * 32 + lane;
       if (cidx < n_v) {
         const int g = cidx / C, cc = cidx - g * C;
-        st_stream(dst_row(g, 2) + 8 * cc, val[u]);
+        out.store(dst_row(g, 2) + 8 * cc, val[u]);
       }
     }
   }
+  out.finish();
 }
 
 // Standalone fused_qknorm_rope on contiguous [B*S*H, D]: one warp per token
@@ -569,10 +601,10 @@ extern "C" int h3b_qknorm_rope_pack(void* send, const void* q, const void* k, co
 #define H3B_QPT(DD)                                                                         \
   if (head_dim == DD)                                                                       \
     h3b::qknorm_rope_pack_tok<DD><<<grid, h3b::kTokWarps * 32, 0, stream>>>(                  \
-        o, (const __nv_bfloat16*)q, (const __nv_bfloat16*)k, (const __nv_bfloat16*)v,      \
-        q_row_stride, k_row_stride, v_row_stride, (const __nv_bfloat16*)q_weight,          \
-        (const __nv_bfloat16*)k_weight, cos, sin, rows, (int)heads, hl, (int)rotary_dim,   \
-        q_eps, k_eps);
+        h3b::LocalSend{o, rows, hl}, (const __nv_bfloat16*)q, (const __nv_bfloat16*)k,    \
+        (const __nv_bfloat16*)v, q_row_stride, k_row_stride, v_row_stride,                 \
+        (const __nv_bfloat16*)q_weight, (const __nv_bfloat16*)k_weight, cos, sin, rows,    \
+        (int)heads, (int)rotary_dim, q_eps, k_eps);
     H3B_QPT(64) H3B_QPT(128) H3B_QPT(256)
 #undef H3B_QPT
     return h3b::check_launch("h3b_qknorm_rope_pack");
@@ -643,4 +675,60 @@ extern "C" int h3b_merge_heads(void* out, const void* x, int64_t world, int64_t 
                                                                                rows, inner);
   }
   return h3b::check_launch("h3b_merge_heads");
+}
+
+// Same kernel as the fast path of h3b_qknorm_rope_pack, storing each head row
+// into the receive buffer of the rank that owns the head (peer-mapped).
+extern "C" int h3b_qknorm_rope_pack_p2p(void* const* recv_ptrs, int64_t world,
+                                        int64_t row_offset, int64_t total_rows, const void* q,
+                                        const void* k, const void* v, int64_t q_row_stride,
+                                        int64_t k_row_stride, int64_t v_row_stride,
+                                        const void* q_weight, const void* k_weight,
+                                        const float* cos, const float* sin, int64_t rows,
+                                        int64_t heads, int64_t head_dim, int64_t rotary_dim,
+                                        float q_eps, float k_eps, h3b_stream_t stream) {
+  H3B_REQUIRE(rows >= 0 && heads > 0 && world > 0, "qknorm_rope_pack_p2p: bad shape");
+  H3B_REQUIRE(world <= h3b::kMaxPeers, "qknorm_rope_pack_p2p: at most %d ranks",
+              h3b::kMaxPeers);
+  H3B_REQUIRE(heads % world == 0, "heads (%lld) must divide Ulysses degree (%lld)",
+              (long long)heads, (long long)world);
+  H3B_REQUIRE(rotary_dim >= 0 && rotary_dim <= head_dim && rotary_dim % 2 == 0,
+              "fused qknorm+rope requires an even rotary dimension no wider than the head, "
+              "got rotary_dim=%lld, head_dim=%lld",
+              (long long)rotary_dim, (long long)head_dim);
+  if ((head_dim != 64 && head_dim != 128 && head_dim != 256) || rotary_dim % 16 != 0 ||
+      (head_dim - rotary_dim) % 16 != 0) {
+    h3b::set_error("qknorm_rope_pack_p2p: needs head_dim 64/128/256 and rotary_dim and "
+                   "head_dim - rotary_dim multiples of 16");
+    return H3B_ERR_UNSUPPORTED;
+  }
+  H3B_REQUIRE(row_offset >= 0 && rows <= total_rows - row_offset,
+              "qknorm_rope_pack_p2p: rows [%lld, %lld) outside the %lld-row receive buffers",
+              (long long)row_offset, (long long)(row_offset + rows), (long long)total_rows);
+  H3B_REQUIRE(recv_ptrs != nullptr, "qknorm_rope_pack_p2p: null receive pointer array");
+  h3b::PeerPtrs ptrs{};
+  for (int i = 0; i < world; ++i) {
+    ptrs.p[i] = recv_ptrs[i];
+    H3B_REQUIRE(ptrs.p[i] != nullptr && aligned16(ptrs.p[i]),
+                "qknorm_rope_pack_p2p: receive buffer %d is null or not 16-byte aligned", i);
+  }
+  if (rows == 0) return H3B_OK;
+  H3B_REQUIRE(aligned16(q) && aligned16(k) && aligned16(v) && aligned16(q_weight) &&
+                  aligned16(k_weight) && q_row_stride % 8 == 0 && k_row_stride % 8 == 0 &&
+                  v_row_stride % 8 == 0 &&
+                  (rotary_dim == 0 || (aligned16(cos) && aligned16(sin))),
+              "qknorm_rope_pack_p2p: tensors must be 16-byte aligned with row strides "
+              "divisible by 8");
+  const int hl = (int)(heads / world);
+  const unsigned grid = (unsigned)((rows + h3b::kTokWarps - 1) / h3b::kTokWarps);
+#define H3B_QPP(DD)                                                                         \
+  if (head_dim == DD)                                                                       \
+    h3b::qknorm_rope_pack_tok<DD><<<grid, h3b::kTokWarps * 32, 0, stream>>>(                  \
+        h3b::PeerRecv{ptrs, row_offset, hl}, (const __nv_bfloat16*)q,                       \
+        (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, q_row_stride, k_row_stride,     \
+        v_row_stride, (const __nv_bfloat16*)q_weight, (const __nv_bfloat16*)k_weight, cos, \
+        sin, rows, (int)heads, (int)rotary_dim, q_eps, k_eps);
+  H3B_QPP(64) H3B_QPP(128) H3B_QPP(256)
+#undef H3B_QPP
+  return h3b::check_launch("h3b_qknorm_rope_pack_p2p");
 }

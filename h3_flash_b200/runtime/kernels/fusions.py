@@ -180,17 +180,9 @@ def fused_gelu_tanh(x):
     return output.view(x.shape)
 
 
-def fused_qknorm_rope_pack(q, k, v, q_weight, k_weight, cos, sin, world, q_eps, k_eps,
-                           out=None):
-    """QK-norm+RoPE of q and k fused with the packed-Ulysses destination-major pack.
+def qknorm_rope_pack_args(op, q, k, v, q_weight, k_weight, cos, sin, world):
+    """Checks shared by the packing ops; returns (rotary_dim, cos fp32, sin fp32)."""
 
-    q, k, v: [rows, heads, head_dim] with contiguous heads inside a row (row stride
-    free, e.g. views into one fused QKV projection). cos/sin: [rows, rotary_dim] or
-    None (norm only). Returns [world, rows, heads/world, 3*head_dim] equal to
-    ``pack_qkv_destination_major(fused_qknorm_rope(q), fused_qknorm_rope(k), v, world)``
-    (src/h3_flash/runtime/parallel/packed_ulysses.py:178-200)."""
-
-    op = "fused_qknorm_rope_pack"
     rows, heads, head_dim = q.shape
     if heads % world:
         raise ValueError(f"heads ({heads}) must divide Ulysses degree ({world})")
@@ -202,17 +194,31 @@ def fused_qknorm_rope_pack(q, k, v, q_weight, k_weight, cos, sin, world, q_eps, 
         if t.stride(-1) != 1 or t.stride(-2) != head_dim:
             raise ValueError(f"{op}: heads must be contiguous within a row")
     if cos is None:
-        rotary_dim = 0
-        cos32 = sin32 = torch.empty(0, dtype=torch.float32, device=q.device)
-    else:
-        rotary_dim = cos.shape[-1]
-        if rotary_dim > head_dim or rotary_dim % 2:
-            raise ValueError(
-                "fused qknorm+rope requires an even rotary dimension no wider "
-                f"than the head, got rotary_dim={rotary_dim}, head_dim={head_dim}"
-            )
-        cos32 = cos.to(torch.float32).contiguous()
-        sin32 = sin.to(torch.float32).contiguous()
+        empty = torch.empty(0, dtype=torch.float32, device=q.device)
+        return 0, empty, empty
+    rotary_dim = cos.shape[-1]
+    if rotary_dim > head_dim or rotary_dim % 2:
+        raise ValueError(
+            "fused qknorm+rope requires an even rotary dimension no wider "
+            f"than the head, got rotary_dim={rotary_dim}, head_dim={head_dim}"
+        )
+    return rotary_dim, cos.to(torch.float32).contiguous(), sin.to(torch.float32).contiguous()
+
+
+def fused_qknorm_rope_pack(q, k, v, q_weight, k_weight, cos, sin, world, q_eps, k_eps,
+                           out=None):
+    """QK-norm+RoPE of q and k fused with the packed-Ulysses destination-major pack.
+
+    q, k, v: [rows, heads, head_dim] with contiguous heads inside a row (row stride
+    free, e.g. views into one fused QKV projection). cos/sin: [rows, rotary_dim] or
+    None (norm only). Returns [world, rows, heads/world, 3*head_dim] equal to
+    ``pack_qkv_destination_major(fused_qknorm_rope(q), fused_qknorm_rope(k), v, world)``
+    (src/h3_flash/runtime/parallel/packed_ulysses.py:178-200)."""
+
+    op = "fused_qknorm_rope_pack"
+    rotary_dim, cos32, sin32 = qknorm_rope_pack_args(op, q, k, v, q_weight, k_weight, cos, sin,
+                                                     world)
+    rows, heads, head_dim = q.shape
     hl = heads // world
     if out is None:
         out = torch.empty((world, rows, hl, 3 * head_dim), dtype=q.dtype, device=q.device)

@@ -13,6 +13,11 @@ W ranks, r local rows, H heads, hl = H/W:
 
 The reference's separate QK-norm+RoPE launches and its standalone pack kernel
 are fused into one kernel. Row counts are exchanged once per request.
+
+With ``exchange="p2p"`` the two NCCL all-to-alls, the send buffer and the
+merge are replaced by peer stores over NVLink (peer_exchange.py): the pack
+kernel writes each head row into its owner's receive buffer and a scatter
+kernel writes each output row into its owner's merged buffer.
 """
 
 from __future__ import annotations
@@ -33,7 +38,9 @@ from .relayout import can_pack_qkv, merge_heads, pack_qkv_destination_major
 class PackedUlyssesRuntime:
     """Request-scoped shape metadata and auditable counters (packed_ulysses.py:19-64)."""
 
-    def __init__(self, group: Any) -> None:
+    def __init__(self, group: Any, exchange: str = "nccl") -> None:
+        if exchange not in ("nccl", "p2p"):
+            raise ValueError(f"exchange must be 'nccl' or 'p2p', got {exchange!r}")
         self.group = group
         self.world = dist.get_world_size(group)
         self._row_counts: tuple[list[int], int] | None = None
@@ -41,6 +48,14 @@ class PackedUlyssesRuntime:
         self.attention_calls = 0
         backend = dist.get_backend(group)
         self._count_device = "cuda" if str(backend) == "nccl" else "cpu"
+        self.exchange = exchange
+        self.peer = None
+        if exchange == "p2p":
+            if not torch.cuda.is_available():
+                raise RuntimeError("the p2p exchange needs CUDA devices")
+            from .peer_exchange import PeerExchange
+
+            self.peer = PeerExchange(group)
 
     def begin_request(self) -> None:
         # Every rank calls this at the same request boundary; the next attention
@@ -69,9 +84,11 @@ class PackedUlyssesRuntime:
             "backend": "packed_ulysses_h3b",
             "degree": self.world,
             "semantics": "dense",
+            "exchange": self.exchange,
             "qkv_collectives_per_attention": 1,
             "output_collectives_per_attention": 1,
-            "relayout": "cuda_fused_qknorm_rope_pack",
+            "relayout": "cuda_fused_qknorm_rope_pack" if self.peer is None
+            else "cuda_fused_qknorm_rope_pack_p2p",
             "attention": "h3b_tcgen05",
             "row_count_collectives_per_request": 1,
             "requests": self.requests,
@@ -206,9 +223,16 @@ def ulysses_attention_forward(attention: Any, hidden_states: torch.Tensor, rotar
         raise ValueError(f"heads ({heads}) must divide Ulysses degree ({world})")
     with TIMER.section("gemm"):
         q, k, v = qkv_projection(attention, hidden_states.reshape(rows_local, -1))
+    norm_q, norm_k = _norm_params(attention.norm_q), _norm_params(attention.norm_k)
+    cos, sin = rotary_emb if rotary_emb is not None else (None, None)
+    if (world > 1 and runtime.peer is not None and fused_qknorm_rope and norm_q is not None
+            and norm_k is not None and _p2p_supported(head_dim, cos)):
+        output = _peer_attention(runtime, q, k, v, norm_q, norm_k, cos, sin, rows_local, head_dim)
+        output = output.reshape(batch, rows_local, heads * head_dim).type_as(hidden_states)
+        runtime.attention_calls += 1
+        with TIMER.section("gemm"):
+            return attention.to_out[1](attention.to_out[0](output))
     with TIMER.section("qknorm_rope_pack"):
-        norm_q, norm_k = _norm_params(attention.norm_q), _norm_params(attention.norm_k)
-        cos, sin = rotary_emb if rotary_emb is not None else (None, None)
         if fused_qknorm_rope and norm_q is not None and norm_k is not None:
             send = fused_qknorm_rope_pack(q, k, v, norm_q[0], norm_k[0], cos, sin, world,
                                           norm_q[1], norm_k[1])
@@ -238,13 +262,41 @@ def ulysses_attention_forward(attention: Any, hidden_states: torch.Tensor, rotar
         return attention.to_out[1](attention.to_out[0](output))
 
 
-def install_packed_ulysses(transformer: Any, *, group: Any = None, fused_qknorm_rope: bool = True) -> PackedUlyssesRuntime:
-    """Replace each block's attention forward with the packed-Ulysses path (packed_ulysses.py:131-220)."""
+def _p2p_supported(head_dim: int, cos: Any) -> bool:
+    rotary_dim = 0 if cos is None else cos.shape[-1]
+    return head_dim in (64, 128, 256) and rotary_dim % 16 == 0 and (head_dim - rotary_dim) % 16 == 0
+
+
+def _peer_attention(runtime: PackedUlyssesRuntime, q, k, v, norm_q, norm_k, cos, sin,
+                    rows_local: int, head_dim: int) -> torch.Tensor:
+    """pack_p2p -> barrier -> attention -> scatter_p2p -> barrier. Returns [r, H, D]."""
+
+    peer = runtime.peer
+    counts = runtime.row_counts(rows_local)
+    with TIMER.section("qknorm_rope_pack"):
+        peer.pack(q, k, v, norm_q[0], norm_k[0], cos, sin, norm_q[1], norm_k[1], counts)
+    with TIMER.section("all_to_all"):
+        peer.barrier()
+    heads_local = q.shape[1] // runtime.world
+    with TIMER.section("attention"):
+        output = packed_attention(peer.recv_view(sum(counts), heads_local, head_dim), head_dim)
+    with TIMER.section("all_to_all"):
+        merged = peer.scatter(output, counts)
+        peer.barrier()
+    return merged
+
+
+def install_packed_ulysses(transformer: Any, *, group: Any = None, fused_qknorm_rope: bool = True,
+                           exchange: str = "nccl") -> PackedUlyssesRuntime:
+    """Replace each block's attention forward with the packed-Ulysses path (packed_ulysses.py:131-220).
+
+    ``exchange="p2p"`` moves rows with peer stores over NVLink instead of NCCL
+    all-to-alls (one process per GPU on one node, CUDA IPC available)."""
 
     if not (dist.is_available() and dist.is_initialized()):
         raise RuntimeError("packed Ulysses requires an initialized process group")
     group = group or dist.group.WORLD
-    runtime = PackedUlyssesRuntime(group)
+    runtime = PackedUlyssesRuntime(group, exchange=exchange)
     if runtime.world < 2:
         raise RuntimeError("packed Ulysses degree must be at least two")
 

@@ -30,7 +30,7 @@ typedef struct CUstream_st* h3b_stream_t; /* == cudaStream_t */
 #define H3B_ERR_CUDA 2        /* CUDA launch or driver error: RuntimeError         */
 #define H3B_ERR_UNSUPPORTED 3 /* valid input this build does not handle: RuntimeError */
 
-#define H3B_ABI_VERSION 2
+#define H3B_ABI_VERSION 3
 
 int h3b_abi_version(void);
 /* Message of the last failing call on this host thread ("" if none). */
@@ -40,7 +40,8 @@ const char* h3b_last_error(void);
  * device. Bounded waits inside kernels that time out OR a bit into it instead of
  * spinning forever. h3b_device_status() copies it to the host (synchronous);
  * h3b_clear_device_status() zeroes it (stream-ordered). Bits:
- *   1 = attention pipeline wait timed out. */
+ *   1 = attention pipeline wait timed out;
+ *   2 = h3b_peer_barrier gave up waiting for a peer (10 s). */
 int h3b_device_status(int* status_out);
 int h3b_clear_device_status(h3b_stream_t stream);
 
@@ -190,6 +191,67 @@ int h3b_attention_noalloc(void* out, const void* q, const void* k, const void* v
                           int64_t v_batch_stride, int64_t v_row_stride, int64_t v_head_stride,
                           int64_t o_batch_stride, int64_t o_row_stride, int64_t o_head_stride,
                           float softmax_scale, h3b_stream_t stream);
+
+/* ---------------------------------------------------------------------------
+ * Packed-Ulysses exchange over NVLink peer memory. Each rank owns one receive
+ * buffer [S_total, hl, 3*head_dim], one merged buffer [rows_local, heads,
+ * head_dim] and one flag array of h3b_peer_flags_bytes() zeroed bytes, all in
+ * device memory it exports with h3b_ipc_handle; every rank opens the others'
+ * with h3b_ipc_open (plain peer mappings). `*_ptrs` arrays are
+ * host arrays of `world` device pointers indexed by rank, this rank's own
+ * local pointer included; world <= 16. One attention call on every rank runs,
+ * on one stream:
+ *   h3b_qknorm_rope_pack_p2p -> h3b_peer_barrier -> h3b_attention on the own
+ *   receive buffer -> h3b_scatter_heads_p2p -> h3b_peer_barrier
+ * and then reads its merged buffer. With that order single buffers are safe
+ * across consecutive calls. All ranks must make the same calls in the same
+ * order.
+ * ------------------------------------------------------------------------- */
+
+/* h3b_qknorm_rope_pack with the pack's store going straight to the owner of
+ * each head: row r of this rank (global row row_offset + r) of head
+ * g = dst*hl + lh lands at recv_ptrs[dst][((row_offset + r)*hl + lh)*3*head_dim].
+ * Needs head_dim 64/128/256, rotary_dim and head_dim - rotary_dim multiples of
+ * 16 (else H3B_ERR_UNSUPPORTED).
+ * replaces the pack + QKV exchange of _packed_qkv_all_to_all
+ *          src/h3_flash/runtime/parallel/packed_ulysses.py:85-108
+ *          (pack_qkv_destination_major relayout.py:97-130) */
+int h3b_qknorm_rope_pack_p2p(void* const* recv_ptrs, int64_t world, int64_t row_offset,
+                             int64_t total_rows, const void* q, const void* k, const void* v,
+                             int64_t q_row_stride, int64_t k_row_stride, int64_t v_row_stride,
+                             const void* q_weight, const void* k_weight, const float* cos,
+                             const float* sin, int64_t rows, int64_t heads, int64_t head_dim,
+                             int64_t rotary_dim, float q_eps, float k_eps, h3b_stream_t stream);
+
+/* out is this rank's attention output [S_total, heads_local, head_dim]
+ * (contiguous); global row s, owned by rank o (row_counts[] gives every rank's
+ * rows in rank order), goes to
+ *   merged_ptrs[o][((s - offset_o)*world + rank)*heads_local*head_dim].
+ * replaces _packed_output_all_to_all  packed_ulysses.py:111-128
+ *          (exchange + merge_heads relayout.py:133-159) */
+int h3b_scatter_heads_p2p(void* const* merged_ptrs, const int64_t* row_counts, const void* out,
+                          int64_t world, int64_t rank, int64_t heads_local, int64_t head_dim,
+                          h3b_stream_t stream);
+
+/* Cross-rank barrier on the ranks' flag arrays; orders every earlier store of
+ * this stream before every later load of the peers' streams. The epoch lives
+ * in the flag array, so the call can be captured in a CUDA graph. A peer
+ * missing for 10 s sets status bit 2 and the kernel returns.
+ * replaces the synchronisation inside dist.all_to_all_single (packed_ulysses.py:67-82) */
+int h3b_peer_barrier(void* const* flag_ptrs, int64_t world, int64_t rank, h3b_stream_t stream);
+int64_t h3b_peer_flags_bytes(void);
+
+/* CUDA IPC for the buffers above. h3b_ipc_handle writes the 64-byte handle of
+ * the allocation holding `ptr` and ptr's offset into it; h3b_ipc_open maps a
+ * peer's handle into this process (on the current device) and returns the
+ * mapped base + offset; h3b_ipc_close drops it. A handle opened again in the
+ * same process shares the first mapping (reference-counted), so buffers carved
+ * out of one allocation can be exported separately. No reference counterpart:
+ * the reference exchanges through NCCL only. */
+#define H3B_IPC_HANDLE_BYTES 64
+int h3b_ipc_handle(const void* ptr, void* handle, int64_t* offset);
+int h3b_ipc_open(const void* handle, int64_t offset, void** ptr);
+int h3b_ipc_close(void* ptr, int64_t offset);
 
 #ifdef __cplusplus
 }
