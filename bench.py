@@ -541,7 +541,7 @@ def main() -> int:
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["h3b", "reference"], default="h3b")
     parser.add_argument("--config", default="480p-5s")
-    parser.add_argument("--exchange", choices=["nccl", "p2p"], default="nccl",
+    parser.add_argument("--exchange", choices=["nccl", "p2p"], default="p2p",
                         help="packed-Ulysses row exchange for N>1: NCCL all-to-all or NVLink peer stores")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--sweep", choices=["elementwise"], help="print the config-2 kernel sweep instead")

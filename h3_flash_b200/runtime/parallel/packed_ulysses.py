@@ -22,6 +22,7 @@ kernel writes each output row into its owner's merged buffer.
 
 from __future__ import annotations
 
+import socket
 from typing import Any
 
 import torch
@@ -286,16 +287,29 @@ def _peer_attention(runtime: PackedUlyssesRuntime, q, k, v, norm_q, norm_k, cos,
     return merged
 
 
+def _single_node_cuda_group(group: Any) -> bool:
+    """True when every rank of ``group`` is a CUDA process on this host (collective)."""
+
+    if str(dist.get_backend(group)) != "nccl" or not torch.cuda.is_available():
+        return False
+    names: list[Any] = [None] * dist.get_world_size(group)
+    dist.all_gather_object(names, socket.gethostname(), group=group)
+    return len(set(names)) == 1
+
+
 def install_packed_ulysses(transformer: Any, *, group: Any = None, fused_qknorm_rope: bool = True,
-                           exchange: str = "nccl") -> PackedUlyssesRuntime:
+                           exchange: str = "auto") -> PackedUlyssesRuntime:
     """Replace each block's attention forward with the packed-Ulysses path (packed_ulysses.py:131-220).
 
-    ``exchange="p2p"`` moves rows with peer stores over NVLink instead of NCCL
-    all-to-alls (one process per GPU on one node, CUDA IPC available)."""
+    ``exchange``: ``"p2p"`` moves rows with peer stores over NVLink (one process
+    per GPU on one node, CUDA IPC available), ``"nccl"`` with NCCL all-to-alls;
+    ``"auto"`` (collective) picks p2p when all ranks are NCCL ranks on one host."""
 
     if not (dist.is_available() and dist.is_initialized()):
         raise RuntimeError("packed Ulysses requires an initialized process group")
     group = group or dist.group.WORLD
+    if exchange == "auto":
+        exchange = "p2p" if _single_node_cuda_group(group) else "nccl"
     runtime = PackedUlyssesRuntime(group, exchange=exchange)
     if runtime.world < 2:
         raise RuntimeError("packed Ulysses degree must be at least two")

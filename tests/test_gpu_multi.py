@@ -80,7 +80,7 @@ def _worker(rank, world, port, queue):
         sp_block = init_block_(H3TransformerBlock(dim=dim, heads=heads, head_dim=128, ffn_inner=4 * dim), seed=5)
         sp_stack = H3BlockStack([sp_block.to("cuda", torch.bfloat16)])
         install_transformer_fusions(sp_stack)
-        sp_runtime = install_packed_ulysses(sp_stack)
+        sp_runtime = install_packed_ulysses(sp_stack, exchange="nccl")
         sp_runtime.begin_request()
         start, stop = split_bounds(total, world, rank)
         with torch.no_grad():
