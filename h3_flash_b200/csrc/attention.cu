@@ -4,28 +4,28 @@
 // One CTA owns two 128-row query tiles of one (batch, head) and streams the
 // whole key/value sequence in 128-row blocks:
 //
-//   warp 16     TMA producer: Q0, Q1 once, then K_j / V_j into separate rings
-//               (2 K stages, 2 V stages, 32 KB each, 128B-swizzled).
-//   warp 17     MMA issuer (one thread): S_t = Q_t K_j^T into TMEM, then
+//   warp 8      TMA producer: Q0, Q1 once, then K_j / V_j into separate rings
+//               (K and V stages of 32 KB each, 128B-swizzled).
+//   warp 9      MMA issuer (one thread): S_t = Q_t K_j^T into TMEM, then
 //               O_t += P_t V_j with P_t read from TMEM (A operand) and V_j from
 //               shared memory (MN-major B operand), in two 64-key halves. Tiles
-//               t=0,1 alternate so the tensor core works on one tile while the
+//               t=0,1 alternate, so the tensor core works on one tile while the
 //               other tile's softmax runs.
-//   warps 0-7   softmax of tile 0, warps 8-15 softmax of tile 1. Warp w owns
-//               TMEM lane quadrant w%4 (query rows 32(w%4)..+31) and key half
-//               (w/4)%2 of every block: two warps share each row, so each SMSP
-//               runs two softmax warps per tile and hides the TMEM/MUFU
-//               latencies of one with the other. Per block a warp streams its 64
-//               S columns from TMEM twice (pass 1: row max, exchanged with the
-//               partner warp through shared memory; pass 2: p = 2^(s*c - m)),
-//               writes P (bf16) over the S columns it has consumed and
-//               accumulates its share of the row sum in fp32. O is rescaled in
-//               TMEM only when the running max grows by more than 2^8 (P stays
+//   warps 0-3   softmax of tile 0, warps 4-7 softmax of tile 1. Warp w owns
+//               TMEM lane quadrant w%4, and each of its threads owns one query
+//               row: it loads the row's 128 scores of a block from TMEM, takes
+//               the row max itself (no exchange between threads), computes
+//               p = 2^(s*c - m), writes P (bf16) over the S columns it has
+//               read and keeps the row sum in fp32. Part of the exponentials
+//               run as a polynomial on the FMA pipe so that the MUFU and the
+//               issue slots of an SMSP share the work. O is rescaled in TMEM
+//               only when the running max grows by more than 2^8 (P stays
 //               <= 256, exact in the fp32 accumulator), which after the first
 //               blocks is rare.
 //
 // TMEM (512 columns): S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512).
-// P of key half h of tile t lives in S_t columns [64h, 64h+32).
+// P of tile t, keys [64h, 64h+64), lives in S_t columns [32h, 32h+32): key k
+// in column k/2 (even key in the low half), the layout the TS-form MMA reads.
 // A tcgen05.commit tracks every earlier MMA of the issuing thread, so the
 // commit after S_t(j) also certifies that PV_t(j-1) is done: the softmax may
 // touch O_t once it has seen S_t(j).
@@ -53,9 +53,12 @@ constexpr int kBlockM = 128;  // query rows per tile
 constexpr int kBlockN = 128;  // key rows per block
 constexpr int kHeadDim = 128;
 constexpr int kTiles = 2;  // query tiles per CTA
-constexpr int kKStages = 2;
+#ifndef H3B_ATTN_K_STAGES
+#define H3B_ATTN_K_STAGES 2
+#endif
+constexpr int kKStages = H3B_ATTN_K_STAGES;
 constexpr int kVStages = 2;
-constexpr int kSoftmaxWarps = 16;  // 8 per query tile: 4 TMEM lane quadrants x 2 key halves
+constexpr int kSoftmaxWarps = 4 * kTiles;  // one per TMEM lane quadrant per tile
 constexpr int kThreads = (kSoftmaxWarps + 2) * 32;  // + TMA warp + MMA warp
 constexpr int kLoadWarp = kSoftmaxWarps;
 constexpr int kMmaWarp = kSoftmaxWarps + 1;
@@ -66,13 +69,11 @@ constexpr uint32_t kSmemQ = 0;
 constexpr uint32_t kSmemK = kSmemQ + kTiles * kTileBytes;
 constexpr uint32_t kSmemV = kSmemK + kKStages * kTileBytes;
 constexpr uint32_t kSmemBar = kSmemV + kVStages * kTileBytes;
-// barriers: q[2], kfull, kempty, vfull, vempty, s[2], p[2][2], o[2], x[2][4] + tmem slot + abort
-constexpr uint32_t kNumBars = kTiles + 2 * kKStages + 2 * kVStages + 4 * kTiles + 4 * kTiles;
-// Row-max / row-sum exchange between the four warps that share a TMEM lane
-// quadrant: float [tile][parity][key segment 4][128 rows].
-constexpr uint32_t kSmemXch = kSmemBar + ((kNumBars * 8 + 16 + 127) / 128) * 128;
-constexpr uint32_t kSmemBytes = kSmemXch + kTiles * 2 * 4 * kBlockM * 4;
+// barriers: q[2], kfull, kempty, vfull, vempty, s[2], p[2][2], o[2] + tmem slot + abort
+constexpr uint32_t kNumBars = kTiles + 2 * kKStages + 2 * kVStages + 4 * kTiles;
+constexpr uint32_t kSmemBytes = kSmemBar + ((kNumBars * 8 + 16 + 127) / 128) * 128;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;  // slack to 1024-align the base
+static_assert(kSmemAlloc <= 232448, "shared memory per CTA");
 
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemS = 0;    // + t*128
@@ -83,12 +84,14 @@ constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
 // Rescale O only when the running row max (log2 units) grew by more than this.
 constexpr float kRescaleThreshold = 8.0f;
 
-// Of every 8 column pairs of S, this many take the FMA-pipe exp2 (exp2_poly)
-// instead of MUFU ex2: the softmax of one 128x128 block needs as many MUFU
-// cycles as the tensor core needs for that tile's two MMAs, so part of the
-// exponentials must move to the (otherwise idle) FMA pipe.
+// Of every 8 column pairs of a row, this many take the FMA-pipe exp2
+// (exp2_poly) instead of MUFU ex2. The MUFU time of one tile's softmax is
+// close to the tensor time of the other tile's MMAs, which the offload
+// shortens; but in this kernel the softmax finishes ahead of the MMA warp and
+// the extra FMA-pipe instructions slow the SMSP that issues the MMAs, so the
+// measured optimum is 0 (kept as a build-time knob).
 #ifndef H3B_ATTN_POLY_PAIRS
-#define H3B_ATTN_POLY_PAIRS 2
+#define H3B_ATTN_POLY_PAIRS 0
 #endif
 constexpr int kPolyPairs = H3B_ATTN_POLY_PAIRS;
 
@@ -418,17 +421,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto bar_vfull = [&](int s) { return bars + 8u * (kTiles + 2 * kKStages + s); };
   auto bar_vempty = [&](int s) { return bars + 8u * (kTiles + 2 * kKStages + kVStages + s); };
   auto bar_s = [&](int t) { return bars + 8u * (kTiles + 2 * kKStages + 2 * kVStages + t); };
-  // bar_p(t, h): softmax of tile t has written P for keys [64h, 64h+64) of the block.
+  // bar_p(t, h): the softmax of tile t has written P for keys [64h, 64h+64) of the block.
   auto bar_p = [&](int t, int h) {
     return bars + 8u * (kTiles + 2 * kKStages + 2 * kVStages + kTiles + 2 * t + h);
   };
   auto bar_o = [&](int t) {
     return bars + 8u * (kTiles + 2 * kKStages + 2 * kVStages + 3 * kTiles + t);
-  };
-  // bar_x(t, quad): the four softmax warps of a lane quadrant have published their
-  // partial row maxima of tile t for this block.
-  auto bar_x = [&](int t, int quad) {
-    return bars + 8u * (kTiles + 2 * kKStages + 2 * kVStages + 4 * kTiles + 4 * t + quad);
   };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemBar + kNumBars * 8);
   volatile uint32_t* abort_flag = tmem_slot + 1;
@@ -454,10 +452,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = 0; t < kTiles; ++t) {
       mbar_init(bar_q(t), 1);
       mbar_init(bar_s(t), 1);
-      mbar_init(bar_p(t, 0), 256);
-      mbar_init(bar_p(t, 1), 256);
+      mbar_init(bar_p(t, 0), 4 * 32);
+      mbar_init(bar_p(t, 1), 4 * 32);
       mbar_init(bar_o(t), 1);
-      for (int qd = 0; qd < 4; ++qd) mbar_init(bar_x(t, qd), 128);
     }
     for (int s = 0; s < kKStages; ++s) {
       mbar_init(bar_kfull(s), 1);
@@ -543,16 +540,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_ss(d, qd + off, kd + off, idesc_qk, kk > 0 ? 1u : 0u);
         }
       };
-      // O_t += P_t V_j over keys [64h, 64h+64): 4 MMAs of K=16.
+      // O_t += P_t V_j over keys [64h, 64h+64): 4 MMAs of K=16; P of keys
+      // [16kk, 16kk+16) is S_t columns [8kk, 8kk+8).
       auto issue_pv = [&](int t, int j, int h) {
         const uint64_t vd = v_desc0 + (uint64_t)(((j % kVStages) * kTileBytes) >> 4);
         const uint32_t d = tmem + kTmemO + t * 128;
 #pragma unroll
         for (int k4 = 0; k4 < kBlockN / 32; ++k4) {
           const int kk = h * (kBlockN / 32) + k4;
-          // keys 16kk..16kk+15 = segment kk/2, second 16 of it if kk is odd
-          mma_ts(d, tmem + kTmemS + t * 128 + (kk >> 1) * 32 + (kk & 1) * 8,
-                 vd + (uint64_t)((kk * 2048) >> 4), idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(d, tmem + kTmemS + t * 128 + kk * 8, vd + (uint64_t)((kk * 2048) >> 4),
+                 idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         }
       };
       if (ok) ok = wait_bar(bar_kfull(0), 0, abort_flag, prm.status);
@@ -596,156 +593,149 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
   } else {
-    // ---------------- softmax: all 16 warps on whichever tile is ready ----------------
-    // Warp w owns TMEM lane quadrant w%4 (query rows 32(w%4)..+31) and key segment
-    // w/4 (block keys [32 seg, 32 seg + 32)) of BOTH tiles; per block it first does
-    // tile 0, then tile 1, so while the MMA warp works on one tile every softmax
-    // warp works on the other (four warps per SMSP share the latency hiding).
+    // ---------------- softmax: warp -> (tile, lane quadrant), thread -> query row ----------------
+    const int t = warp >> 2;
     const int quad = warp & 3;
-    const int seg = warp >> 2;
-    const int hk = seg >> 1;  // key half whose P barrier this warp arrives on
     const int row_in_tile = quad * 32 + lane;
     const uint32_t lanes = (uint32_t)(quad * 32) << 16;
-    float* xch = reinterpret_cast<float*>(smem + kSmemXch);
-    auto xslot = [&](int t, int parity, int sg) {
-      return xch + ((t * 2 + parity) * 4 + sg) * kBlockM + row_in_tile;
-    };
-    const uint32_t quad_bar = 1 + quad;  // named barrier of the four warps on these rows
+    const uint32_t t_s = tmem + lanes + kTmemS + t * 128;
+    const uint32_t t_o = tmem + lanes + kTmemO + t * 128;
     const float c = prm.scale_log2;
-    float m_use[kTiles] = {-INFINITY, -INFINITY};
-    float l_sum[kTiles] = {0.f, 0.f};
+    float m_use = -INFINITY;  // running row max, log2 units, that P is taken against
+    float l_sum = 0.f;
     bool ok = true;
     for (int j = 0; j < n_kv && ok; ++j) {
-#pragma unroll
-      for (int t = 0; t < kTiles; ++t) {
-        const uint32_t t_s = tmem + lanes + kTmemS + t * 128 + seg * 32;  // this warp's S columns
-        const uint32_t t_o = tmem + lanes + kTmemO + t * 128 + seg * 32;  // and O columns
-        ok = wait_bar(bar_s(t), j & 1, abort_flag, prm.status);
-        // tcgen05.ld/st below are warp-collective; the named barrier is quad-collective.
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-        tc_fence_after();
-        const int valid = prm.seq_k - (j0 + j) * kBlockN - seg * 32;  // keys of this segment
-        // One TMEM pass: the warp's 32 columns of S, in two 16-column loads.
-        uint32_t sv[2][16];
-        tmem_ld16(t_s, sv[0]);
-        tmem_ld16(t_s + 16, sv[1]);
-        tmem_ld_wait16(sv[0]);
-        tmem_pin16(sv[1]);
-        if (valid < 32) {
-          mask_keys16(sv[0], 0, valid);
-          mask_keys16(sv[1], 16, valid);
-        }
-        float mxp[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          mxp[i] = max3(__uint_as_float(sv[0][4 * i]), __uint_as_float(sv[0][4 * i + 1]),
-                        __uint_as_float(sv[0][4 * i + 2]));
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          mxp[i] = max3(mxp[i], __uint_as_float(sv[0][4 * i + 3]), __uint_as_float(sv[1][4 * i]));
-          mxp[i] = max3(mxp[i], __uint_as_float(sv[1][4 * i + 1]),
-                        __uint_as_float(sv[1][4 * i + 2]));
-          mxp[i] = fmaxf(mxp[i], __uint_as_float(sv[1][4 * i + 3]));
-        }
-        // Publish this warp's partial max (non-blocking), then exponentiate
-        // against the running max while the quadrant's other warps catch up.
-        *xslot(t, j & 1, seg) = fmaxf(fmaxf(mxp[0], mxp[1]), fmaxf(mxp[2], mxp[3]));
-        mbar_arrive(bar_x(t, quad));
-        // p = 2^(s*c - m) for the 16 column pairs, packed fp32x2; kPolyPairs of
-        // every 8 pairs use the FMA-pipe exp2 so MUFU and FMA share the work.
-        float2 lp[2];
-        uint32_t pk[16];
-        auto exponentiate = [&](float m) {
-          const float2 c2 = make_float2(c, c);
-          const float2 nm2 = make_float2(-m, -m);
-          lp[0] = lp[1] = make_float2(0.f, 0.f);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const uint32_t* src = sv[i >> 3];
-            const int k = (i & 7) * 2;
-            const float2 x = __ffma2_rn(
-                make_float2(__uint_as_float(src[k]), __uint_as_float(src[k + 1])), c2, nm2);
-            float2 p;
-            if ((i & 7) >= 8 - kPolyPairs) {
-              p = exp2_poly(x);
-            } else {
-              p.x = ex2(x.x);
-              p.y = ex2(x.y);
-            }
-            lp[i & 1] = __fadd2_rn(lp[i & 1], p);
-            pk[i] = pack_bf16(p.x, p.y);
-          }
-        };
-        if (j > 0) exponentiate(m_use[t]);
-        ok = wait_bar(bar_x(t, quad), j & 1, abort_flag, prm.status);
-        ok = __all_sync(0xffffffffu, ok);
-        if (!ok) break;
-        const float mx = fmaxf(fmaxf(*xslot(t, j & 1, 0), *xslot(t, j & 1, 1)),
-                               fmaxf(*xslot(t, j & 1, 2), *xslot(t, j & 1, 3)));
-        const float m_new = mx * c;
-        const bool need = m_new > m_use[t] + kRescaleThreshold;  // same in the 4 warps
-        if (__any_sync(0xffffffffu, need)) {
-          if (j > 0) {
-            // PV_t(j-1) is complete: the S_t(j) commit covers every earlier MMA.
-            const float alpha = need ? ex2(m_use[t] - m_new) : 1.f;
-            uint32_t o[32];
-            tmem_ld32(t_o, o);
-            tmem_ld_wait(o);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-            tmem_st32(t_o, o);
-            l_sum[t] *= alpha;
-          }
-          if (need) m_use[t] = m_new;
-          exponentiate(m_use[t]);  // redo against the new running max
-        }
-        // P (bf16) of the 32 keys goes to S columns [32 seg, 32 seg + 16), already read.
-        tmem_st16(t_s, pk);
-        tmem_st_wait();
-        tc_fence_before();
-        mbar_arrive(bar_p(t, hk));
-        l_sum[t] += (lp[0].x + lp[0].y) + (lp[1].x + lp[1].y);
-      }
-    }
-    // ---------------- epilogue: O / l -> bf16 (or fp32 partials) ----------------
-#pragma unroll
-    for (int t = 0; t < kTiles; ++t) {
-      if (!ok) break;
-      const uint32_t t_o = tmem + lanes + kTmemO + t * 128 + seg * 32;
-      ok = wait_bar(bar_o(t), 0, abort_flag, prm.status);
+      ok = wait_bar(bar_s(t), j & 1, abort_flag, prm.status);
+      // tcgen05.ld/st below are warp-collective.
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      // Row sum = the four segments' shares (parity slot after the last exchange).
-      *xslot(t, n_kv & 1, seg) = l_sum[t];
-      named_bar_sync(quad_bar, 128);
-      const float l_row = (*xslot(t, n_kv & 1, 0) + *xslot(t, n_kv & 1, 1)) +
-                          (*xslot(t, n_kv & 1, 2) + *xslot(t, n_kv & 1, 3));
-      uint32_t o[32];
-      tmem_ld32(t_o, o);
-      tmem_ld_wait(o);
-      if (split_slot >= 0) {
-        // Partial result of a key range: unnormalised O and (running max, sum).
-        float* ws = prm.ws + (int64_t)split_slot * kWsSlotFloats + t * kWsTileFloats;
-        float* o_row = ws + row_in_tile * kHeadDim + seg * 32;
+      uint32_t sv[4][32];
 #pragma unroll
-        for (int v4 = 0; v4 < 8; ++v4)
-          *reinterpret_cast<float4*>(o_row + v4 * 4) =
-              make_float4(__uint_as_float(o[v4 * 4 + 0]), __uint_as_float(o[v4 * 4 + 1]),
-                          __uint_as_float(o[v4 * 4 + 2]), __uint_as_float(o[v4 * 4 + 3]));
-        if (seg == 0) {
-          float* ml = ws + kBlockM * kHeadDim + 2 * row_in_tile;
-          ml[0] = m_use[t];
-          ml[1] = l_row;
+      for (int q4 = 0; q4 < 4; ++q4) tmem_ld32(t_s + 32 * q4, sv[q4]);
+      tmem_ld_wait(sv[0]);
+      tmem_pin(sv[1]);
+      tmem_pin(sv[2]);
+      tmem_pin(sv[3]);
+      const int valid = prm.seq_k - (j0 + j) * kBlockN;  // keys of this block that exist
+      if (valid < kBlockN) {
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) mask_keys(sv[q4], 32 * q4, valid);
+      }
+      // p = 2^(s*c - m) in packed fp32x2 for keys [64h, 64h+64); kPolyPairs of
+      // every 8 pairs take the FMA-pipe exp2.
+      const float2 c2 = make_float2(c, c);
+      float2 acc[2];
+      uint32_t pk[32];
+      auto exponentiate = [&](int h, float m) {
+        const float2 nm2 = make_float2(-m, -m);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const int key = 64 * h + 2 * i;
+          const uint32_t* src = sv[key >> 5] + (key & 31);
+          const float2 x =
+              __ffma2_rn(make_float2(__uint_as_float(src[0]), __uint_as_float(src[1])), c2, nm2);
+          float2 p;
+          if ((i & 7) >= 8 - kPolyPairs) {
+            p = exp2_poly(x);
+          } else {
+            p.x = ex2(x.x);
+            p.y = ex2(x.y);
+          }
+          acc[i & 1] = __fadd2_rn(acc[i & 1], p);
+          pk[i] = pack_bf16(p.x, p.y);
         }
-      } else {
-        const float inv_l = 1.f / l_row;
-        const int row = q_row0 + t * kBlockM + row_in_tile;
-        if (row < prm.seq_q) {
-          __nv_bfloat16* dst = prm.out + (int64_t)batch * prm.o_batch_stride +
-                               (int64_t)row * prm.o_row_stride +
-                               (int64_t)head * prm.o_head_stride + seg * 32;
+      };
+      // Row max over the 128 scores (eight independent 3-input max chains) and,
+      // independent of it, the first half of P against the running max: the
+      // scheduler interleaves the two, so the max costs no latency. The half is
+      // redone in the rare case that the max moved by more than the threshold
+      // (always at j = 0, where the running max is still -inf).
+      float mx[8];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) {
+        const uint32_t* r = sv[a >> 1] + (a & 1) * 16;
+        float m = max3(__uint_as_float(r[0]), __uint_as_float(r[1]), __uint_as_float(r[2]));
+#pragma unroll
+        for (int k = 3; k < 15; k += 2) m = max3(m, __uint_as_float(r[k]), __uint_as_float(r[k + 1]));
+        mx[a] = fmaxf(m, __uint_as_float(r[15]));
+      }
+      acc[0] = acc[1] = make_float2(0.f, 0.f);
+      exponentiate(0, m_use);
+      const float row_max = fmaxf(max3(mx[0], mx[1], mx[2]), max3(mx[3], max3(mx[4], mx[5], mx[6]), mx[7]));
+      const float m_new = row_max * c;
+      const bool need = m_new > m_use + kRescaleThreshold;
+      if (__any_sync(0xffffffffu, need)) {
+        const float m_next = need ? m_new : m_use;
+        if (j > 0) {
+          // PV_t(j-1) is complete: the S_t(j) commit covers every earlier MMA.
+          const float alpha = ex2(m_use - m_next);  // 1 for rows that keep their max
+          // 16 columns at a time: the row's 128 scores stay live in registers.
+#pragma unroll 1
+          for (int q8 = 0; q8 < 8; ++q8) {
+            uint32_t o[16];
+            tmem_ld16(t_o + 16 * q8, o);
+            tmem_ld_wait16(o);
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st16(t_o + 16 * q8, o);
+          }
+          l_sum *= alpha;
+        }
+        m_use = m_next;
+        // S columns [0, 64) are still intact: reload them rather than keep the
+        // first half's scores live in registers across this rare branch.
+        tmem_ld32(t_s, sv[0]);
+        tmem_ld32(t_s + 32, sv[1]);
+        tmem_ld_wait(sv[0]);
+        tmem_pin(sv[1]);
+        if (valid < kBlockN) {
+          mask_keys(sv[0], 0, valid);
+          mask_keys(sv[1], 32, valid);
+        }
+        acc[0] = acc[1] = make_float2(0.f, 0.f);
+        exponentiate(0, m_use);
+      }
+      // P of keys [64h, 64h+64) -> S columns [32h, 32h+32), already read.
+      tmem_st32(t_s, pk);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(bar_p(t, 0));
+      exponentiate(1, m_use);
+      tmem_st32(t_s + 32, pk);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(bar_p(t, 1));
+      l_sum += (acc[0].x + acc[0].y) + (acc[1].x + acc[1].y);
+    }
+    // ---------------- epilogue: O / l -> bf16 (or fp32 partials) ----------------
+    if (ok) {
+      ok = wait_bar(bar_o(t), 0, abort_flag, prm.status);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (ok) {
+      tc_fence_after();
+      const int row = q_row0 + t * kBlockM + row_in_tile;
+      const float inv_l = 1.f / l_sum;
+      float* ws = split_slot >= 0
+                      ? prm.ws + (int64_t)split_slot * kWsSlotFloats + t * kWsTileFloats
+                      : nullptr;
+      __nv_bfloat16* dst = prm.out + (int64_t)batch * prm.o_batch_stride +
+                           (int64_t)row * prm.o_row_stride + (int64_t)head * prm.o_head_stride;
+#pragma unroll 1
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint32_t o[32];
+        tmem_ld32(t_o + 32 * q4, o);
+        tmem_ld_wait(o);
+        if (ws != nullptr) {
+          // Partial result of a key range: unnormalised O and (running max, sum).
+          float* o_row = ws + row_in_tile * kHeadDim + 32 * q4;
+#pragma unroll
+          for (int v4 = 0; v4 < 8; ++v4)
+            *reinterpret_cast<float4*>(o_row + v4 * 4) =
+                make_float4(__uint_as_float(o[v4 * 4 + 0]), __uint_as_float(o[v4 * 4 + 1]),
+                            __uint_as_float(o[v4 * 4 + 2]), __uint_as_float(o[v4 * 4 + 3]));
+        } else if (row < prm.seq_q) {
 #pragma unroll
           for (int v8 = 0; v8 < 4; ++v8) {
             uint4 u;
@@ -757,9 +747,14 @@ __global__ void __launch_bounds__(kThreads, 1)
                             __uint_as_float(o[v8 * 8 + 5]) * inv_l);
             u.w = pack_bf16(__uint_as_float(o[v8 * 8 + 6]) * inv_l,
                             __uint_as_float(o[v8 * 8 + 7]) * inv_l);
-            *reinterpret_cast<uint4*>(dst + v8 * 8) = u;
+            *reinterpret_cast<uint4*>(dst + 32 * q4 + v8 * 8) = u;
           }
         }
+      }
+      if (ws != nullptr) {
+        float* ml = ws + kBlockM * kHeadDim + 2 * row_in_tile;
+        ml[0] = m_use;
+        ml[1] = l_sum;
       }
     }
   }
