@@ -202,8 +202,11 @@ def ulysses_case(reference: str) -> dict[str, np.ndarray]:
 
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__)
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", default=os.environ.get("H3_FLASH_REFERENCE"),
+                        help="checkout of fluxmatrix/h3-flash (default: $H3_FLASH_REFERENCE)")
     args = parser.parse_args()
+    if not args.reference:
+        parser.error("pass --reference or set H3_FLASH_REFERENCE")
     src = str(Path(args.reference) / "src")
     sys.path.insert(0, src)
     from h3_flash.runtime.kernels import fusions
