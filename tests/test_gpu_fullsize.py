@@ -1,0 +1,102 @@
+"""Parity at the BASELINE 480p-5s sizes, where the CPU oracle is too slow.
+
+The checks use properties that hold at any size:
+- attention over the full S = 51,200 joint sequence (3 heads: the SP8 per-rank shape, and
+  24 heads: one GPU) agrees with torch's scaled_dot_product_attention. Torch is only the
+  checker here; both are bf16-in, fp32-accumulate.
+- the fused QK-norm+RoPE+pack at the SP8 per-rank shape ([6400, 24, 128], W=8) equals,
+  bit for bit, the standalone fused QK-norm+RoPE followed by the destination-major pack,
+  and the pack then the merge of q is the identity.
+- the fused block at d=3072, S=51,200 agrees with the same module's eager bf16 forward
+  (torch ops and SDPA). Both carry bf16 rounding at every stage (the eager one more), so the
+  bar is set for the difference of two approximations: excess over half a bf16 spacing
+  <= 6e-2, cosine >= 0.9999, relative L2 <= 1e-2.
+"""
+
+from __future__ import annotations
+
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+S = 51200
+
+
+def _metrics(got: torch.Tensor, ref: torch.Tensor):
+    got, ref = got.float(), ref.float()
+    diff = (got - ref).abs()
+    half_ulp = ref.abs().clamp_min(2.0 ** -126) * 2.0 ** -9
+    excess = float((diff - half_ulp).clamp_min(0).max())
+    cosine = float(F.cosine_similarity(got.flatten(), ref.flatten(), dim=0))
+    return float(diff.max()), excess, cosine
+
+
+@pytest.mark.parametrize("heads", [3, 24])
+def test_full_sequence_attention_matches_sdpa(heads):
+    from h3_flash_b200 import _lib
+    from h3_flash_b200.runtime.attention.dense import packed_attention
+
+    g = torch.Generator(device="cuda").manual_seed(heads)
+    packed = torch.randn(S, heads, 384, device="cuda", generator=g).to(torch.bfloat16)
+    out = packed_attention(packed, 128)
+    q, k, v = (packed[..., i * 128 : (i + 1) * 128].permute(1, 0, 2).unsqueeze(0) for i in range(3))
+    ref = F.scaled_dot_product_attention(q, k, v, scale=1.0 / math.sqrt(128))[0].permute(1, 0, 2)
+    torch.cuda.synchronize()
+    max_abs, excess, cosine = _metrics(out, ref)
+    assert torch.isfinite(out).all()
+    # two bf16 computations of the same value: each rounds its output once
+    assert max_abs <= 2e-2 and cosine >= 0.9999, (max_abs, cosine)
+    assert _lib.device_status() == 0
+
+
+def test_sp8_pack_is_bit_exact_and_inverts():
+    from h3_flash_b200.runtime.kernels.fusions import fused_qknorm_rope, fused_qknorm_rope_pack
+    from h3_flash_b200.runtime.parallel.relayout import merge_heads, pack_qkv_destination_major
+    from h3_flash_b200.workloads import CONFIGS, positions, rope_tables
+
+    cfg = CONFIGS["480p-5s"]
+    rows, heads, world = cfg.seq // 8, 24, 8
+    g = torch.Generator(device="cuda").manual_seed(7)
+    qkv = torch.randn(rows, 3 * heads * 128, device="cuda", generator=g).to(torch.bfloat16)
+    q, k, v = (qkv[:, i * heads * 128 : (i + 1) * heads * 128].view(rows, heads, 128) for i in range(3))
+    wq = (1 + 0.02 * torch.randn(128, device="cuda", generator=g)).to(torch.bfloat16)
+    wk = (1 + 0.02 * torch.randn(128, device="cuda", generator=g)).to(torch.bfloat16)
+    cos, sin = (t[:rows].cuda() for t in rope_tables(positions(cfg), cfg.rotary_dim, cfg.theta))
+    fused = fused_qknorm_rope_pack(q, k, v, wq, wk, cos, sin, world, 1e-6, 1e-6)
+    qn = fused_qknorm_rope(q.unsqueeze(0), wq, cos, sin, 1e-6).squeeze(0)
+    kn = fused_qknorm_rope(k.unsqueeze(0), wk, cos, sin, 1e-6).squeeze(0)
+    two_step = pack_qkv_destination_major(qn, kn, v.contiguous(), world)
+    assert torch.equal(fused, two_step)
+    back = merge_heads(fused[..., :128].contiguous())
+    assert torch.equal(back, qn)
+
+
+def test_full_size_block_matches_eager():
+    from h3_flash_b200 import _lib
+    from h3_flash_b200.runtime.h3_block import H3BlockStack, H3TransformerBlock
+    from h3_flash_b200.runtime.kernels import install_transformer_fusions
+    from h3_flash_b200.workloads import CONFIGS, adaln_indices, init_block_, positions, rope_tables
+
+    cfg = CONFIGS["480p-5s"]
+    block = init_block_(H3TransformerBlock(cfg.dim, cfg.heads, cfg.head_dim, cfg.ffn_inner, eps=cfg.eps,
+                                           qk_eps=cfg.eps), seed=0)
+    block = block.to("cuda", torch.bfloat16).eval()
+    stack = H3BlockStack([block])
+    g = torch.Generator().manual_seed(1)
+    hidden = torch.randn(1, cfg.seq, cfg.dim, generator=g).to(torch.bfloat16).cuda()
+    idx = adaln_indices(cfg).cuda()
+    cos, sin = (t.cuda() for t in rope_tables(positions(cfg), cfg.rotary_dim, cfg.theta))
+    with torch.no_grad():
+        eager = stack(hidden, None, idx, (cos, sin))
+        install_transformer_fusions(stack)
+        fused = stack(hidden, None, idx, (cos, sin))
+    torch.cuda.synchronize()
+    max_abs, excess, cosine = _metrics(fused, eager)
+    rel_l2 = float((fused.float() - eager.float()).norm() / eager.float().norm())
+    assert torch.isfinite(fused).all()
+    assert excess <= 6e-2 and cosine >= 0.9999 and rel_l2 <= 1e-2, (max_abs, excess, cosine, rel_l2)
+    assert _lib.device_status() == 0
