@@ -1,12 +1,14 @@
 """Packed-Ulysses exchange over NVLink peer stores (exchange="p2p").
 
-The peer path must reproduce the NCCL path bit for bit: the receive buffer after
-pack_p2p + barrier equals fused_qknorm_rope_pack + all_to_all_single, the merged
-buffer after scatter_p2p + barrier equals all_to_all_single + merge_heads, and a
-block stack run with exchange="p2p" equals the same stack run over NCCL, over
-several requests of different (uneven) row splits, so the buffers are reused and
-regrown. One single-GPU test makes the barrier's bounded wait run out on a flag
-that nothing sets and checks the status bit it leaves.
+The peer path must reproduce the NCCL path bit for bit:
+- the receive buffer after pack_p2p + barrier equals fused_qknorm_rope_pack +
+  all_to_all_single;
+- the merged buffer after scatter_p2p + barrier equals all_to_all_single + merge_heads;
+- a block stack run with exchange="p2p" equals the same stack run over NCCL.
+This holds over several requests of different (uneven) row splits, so the buffers are
+reused and regrown, and for one request in which a rank holds no rows. One single-GPU
+test makes the barrier's bounded wait run out on a flag that nothing sets, and checks
+the status bit it leaves.
 """
 
 from __future__ import annotations
@@ -54,8 +56,9 @@ def _worker(rank, world, port, queue):
         nccl_rt = PackedUlyssesRuntime(dist.group.WORLD)
         p2p_rt = PackedUlyssesRuntime(dist.group.WORLD, exchange="p2p")
         heads = 3 * world
-        for request, base in enumerate((37, 301)):
-            rows = base + 3 * (world - rank)
+        # requests: uneven rows; then larger (the buffers regrow); then rank 0 with no rows
+        for request, base in enumerate((37, 301, 5)):
+            rows = base + 3 * (world - rank) if request < 2 else (0 if rank == 0 else base)
             g = torch.Generator(device="cuda").manual_seed(100 * request + rank)
             qkv = torch.randn(rows, 3 * heads * 128, device="cuda", generator=g).to(torch.bfloat16)
             q, k, v = (qkv[:, i * heads * 128 : (i + 1) * heads * 128].view(rows, heads, 128) for i in range(3))
@@ -79,7 +82,7 @@ def _worker(rank, world, port, queue):
             got_back = peer.scatter(out, counts)
             peer.barrier()
             checks[f"out_{request}"] = bool(torch.equal(got_back, want_back))
-        checks["regrown"] = p2p_rt.peer.reallocations == 2
+        checks["regrown"] = p2p_rt.peer.reallocations == 2  # the third request fits
 
         # 2) a two-block stack, NCCL vs p2p, two requests of different splits
         heads, dim = 2 * world, 256 * world
