@@ -56,24 +56,51 @@ __device__ __forceinline__ unsigned long long globaltimer() {
   return t;
 }
 
-// 16-byte chunks c of the [S_total, hl*D] output: chunk c of global row `row`
-// goes to merged[owner][(row - off[owner]) * W + rank][c - row*inner8].
+// Width in bytes of the chunks the scatter moves per thread: 32 (the 256-bit
+// sm_100 loads/stores, fewer and larger remote writes) when the row width and
+// the buffers allow it, else 16.
+#ifndef H3B_SCATTER_BYTES
+#define H3B_SCATTER_BYTES 32
+#endif
+
+template <int kBytes>
+struct ChunkIO;
+template <>
+struct ChunkIO<16> {
+  using T = uint4;
+  static __device__ __forceinline__ T load(const void* p) { return ld_stream(p); }
+  static __device__ __forceinline__ void store(void* p, const T& v) {
+    *reinterpret_cast<uint4*>(p) = v;
+  }
+};
+template <>
+struct ChunkIO<32> {
+  using T = Chunk32;
+  static __device__ __forceinline__ T load(const void* p) { return ld_stream32(p); }
+  static __device__ __forceinline__ void store(void* p, const T& v) { st32(p, v); }
+};
+
+// kBytes-wide chunks c of the [S_total, hl*D] output: chunk c of global row `row`
+// goes to merged[owner][(row - off[owner]) * W + rank][c - row*inner].
+template <int kBytes>
 __global__ void __launch_bounds__(kScatterThreads) scatter_heads_kernel(
     PeerPtrs merged, RowOffsets offs, const __nv_bfloat16* __restrict__ out, int world,
-    int rank, int64_t total_chunks, int64_t inner8) {
+    int rank, int64_t total_chunks, int64_t inner) {
+  using IO = ChunkIO<kBytes>;
+  constexpr int kElems = kBytes / 2;
   const int64_t base = (int64_t)blockIdx.x * (kScatterThreads * kScatterUnroll) + threadIdx.x;
-  uint4 val[kScatterUnroll];
+  typename IO::T val[kScatterUnroll];
 #pragma unroll
   for (int u = 0; u < kScatterUnroll; ++u) {
     const int64_t c = base + u * kScatterThreads;
-    if (c < total_chunks) val[u] = ld_stream(out + c * 8);
+    if (c < total_chunks) val[u] = IO::load(out + c * kElems);
   }
 #pragma unroll
   for (int u = 0; u < kScatterUnroll; ++u) {
     const int64_t c = base + u * kScatterThreads;
     if (c < total_chunks) {
-      const int64_t row = c / inner8;
-      const int64_t col = c - row * inner8;
+      const int64_t row = c / inner;
+      const int64_t col = c - row * inner;
       // Owner = last rank whose first row is <= row (offsets never decrease).
       int owner = 0;
       int64_t first = 0;
@@ -81,8 +108,8 @@ __global__ void __launch_bounds__(kScatterThreads) scatter_heads_kernel(
       for (int j = 1; j < kMaxPeers; ++j)
         if (j < world && row >= offs.off[j]) owner = j, first = offs.off[j];
       __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(peer_at(merged, owner)) +
-                           (((row - first) * world + rank) * inner8 + col) * 8;
-      *reinterpret_cast<uint4*>(dst) = val[u];
+                           (((row - first) * world + rank) * inner + col) * kElems;
+      IO::store(dst, val[u]);
     }
   }
   __threadfence_system();
@@ -185,14 +212,23 @@ extern "C" int h3b_scatter_heads_p2p(void* const* merged_ptrs, const int64_t* ro
     offs.off[i + 1] = offs.off[i] + row_counts[i];
   }
   for (int i = (int)world + 1; i <= kMaxPeers; ++i) offs.off[i] = offs.off[world];
-  const int64_t inner8 = heads_local * head_dim / 8;
-  const int64_t total_chunks = offs.off[world] * inner8;
-  if (total_chunks == 0) return H3B_OK;
+  const int64_t width = heads_local * head_dim;  // elements of one row of this rank's heads
+  if (offs.off[world] == 0) return H3B_OK;
   H3B_REQUIRE(aligned16(out), "scatter_heads_p2p: out must be 16-byte aligned");
+  bool wide = H3B_SCATTER_BYTES == 32 && width % 16 == 0 && aligned32(out);
+  for (int i = 0; i < world && wide; ++i) wide = aligned32(ptrs.p[i]);
   const int64_t per_block = kScatterThreads * kScatterUnroll;
-  scatter_heads_kernel<<<(unsigned)((total_chunks + per_block - 1) / per_block), kScatterThreads,
-                         0, stream>>>(ptrs, offs, (const __nv_bfloat16*)out, (int)world,
-                                      (int)rank, total_chunks, inner8);
+  if (wide) {
+    const int64_t inner = width / 16, total_chunks = offs.off[world] * inner;
+    scatter_heads_kernel<32><<<(unsigned)((total_chunks + per_block - 1) / per_block),
+                               kScatterThreads, 0, stream>>>(
+        ptrs, offs, (const __nv_bfloat16*)out, (int)world, (int)rank, total_chunks, inner);
+  } else {
+    const int64_t inner = width / 8, total_chunks = offs.off[world] * inner;
+    scatter_heads_kernel<16><<<(unsigned)((total_chunks + per_block - 1) / per_block),
+                               kScatterThreads, 0, stream>>>(
+        ptrs, offs, (const __nv_bfloat16*)out, (int)world, (int)rank, total_chunks, inner);
+  }
   return check_launch("h3b_scatter_heads_p2p");
 }
 
