@@ -616,6 +616,89 @@ def profile_kernel(args) -> None:
     print(f"profile-kernel {args.profile_kernel} done")
 
 
+def exchange_bench(args) -> dict | None:
+    """Per-operation timing of the packed-Ulysses row exchange at the config's shape
+    (N>1 under torchrun): the peer-store path (pack to the owners, barrier, scatter)
+    against NCCL all-to-all of the same rows. CUDA events, max over ranks."""
+
+    import torch.distributed as dist
+
+    from h3_flash_b200.runtime.kernels.fusions import fused_qknorm_rope_pack
+    from h3_flash_b200.runtime.parallel.packed_ulysses import (
+        PackedUlyssesRuntime,
+        _packed_output_all_to_all,
+        packed_qkv_exchange,
+    )
+    from h3_flash_b200.runtime.parallel.peer_exchange import PeerExchange
+    from h3_flash_b200.workloads import CONFIGS, split_sizes
+
+    rank, world, _ = _dist_setup(args.gpus)
+    if world < 2:
+        raise SystemExit("--exchange-bench needs N>1 (launch under torchrun)")
+    cfg = CONFIGS[args.config]
+    heads, dim = cfg.heads, cfg.head_dim
+    counts = split_sizes(cfg.seq, world)
+    rows = counts[rank]
+    g = torch.Generator(device="cuda").manual_seed(rank)
+    qkv = torch.randn(rows, 3 * heads * dim, device="cuda", generator=g).to(torch.bfloat16)
+    q, k, v = (qkv[:, i * heads * dim:(i + 1) * heads * dim].view(rows, heads, dim) for i in range(3))
+    weight = torch.ones(dim, device="cuda", dtype=torch.bfloat16)
+    cos = torch.rand(rows, cfg.rotary_dim, device="cuda", generator=g)
+    sin = torch.rand(rows, cfg.rotary_dim, device="cuda", generator=g)
+    out = torch.randn(cfg.seq, heads // world, dim, device="cuda", generator=g).to(torch.bfloat16)
+    peer = PeerExchange(dist.group.WORLD)
+    runtime = PackedUlyssesRuntime(dist.group.WORLD)
+    runtime.begin_request()
+    runtime.row_counts(rows)
+    send = fused_qknorm_rope_pack(q, k, v, weight, weight, cos, sin, world, cfg.eps, cfg.eps)
+
+    def timed(fn) -> float:
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(args.steps):
+            fn()
+        end.record()
+        torch.cuda.synchronize()
+        return _max_over_ranks(start.elapsed_time(end) / args.steps, world)
+
+    def pack_p2p():
+        peer.pack(q, k, v, weight, weight, cos, sin, cfg.eps, cfg.eps, counts)
+        peer.barrier()
+
+    def scatter_p2p():
+        peer.scatter(out, counts)
+        peer.barrier()
+
+    ms = {
+        "pack_p2p_and_barrier": timed(pack_p2p),
+        "barrier": timed(peer.barrier),
+        "scatter_p2p_and_barrier": timed(scatter_p2p),
+        "pack_local": timed(lambda: fused_qknorm_rope_pack(q, k, v, weight, weight, cos, sin, world,
+                                                           cfg.eps, cfg.eps)),
+        "nccl_qkv_all_to_all": timed(lambda: packed_qkv_exchange(send, rows, runtime)),
+        "nccl_output_all_to_all_and_merge": timed(lambda: _packed_output_all_to_all(out, rows, runtime)),
+    }
+    qkv_remote = max(counts) * heads * 3 * dim * 2 * (world - 1) / world
+    out_remote = cfg.seq * (heads // world) * dim * 2 * (world - 1) / world
+    peer.close()
+    if rank != 0:
+        return None
+    return {
+        "exchange_bench": cfg.name, "n_gpus": world, "steps": args.steps,
+        "ms": {key: round(value, 4) for key, value in ms.items()},
+        "remote_mb_per_rank": {"qkv": round(qkv_remote / 1e6, 2), "output": round(out_remote / 1e6, 2)},
+        "peer_gbs": {
+            "pack": round(qkv_remote / ((ms["pack_p2p_and_barrier"] - ms["barrier"]) * 1e-3) / 1e9, 1),
+            "scatter": round(out_remote / ((ms["scatter_p2p_and_barrier"] - ms["barrier"]) * 1e-3) / 1e9, 1),
+            "peak_measured_peer_copy": NVLINK_PEER_GBS,
+        },
+    }
+
+
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[1])
     parser.add_argument("--gpus", type=int, default=1)
@@ -630,12 +713,22 @@ def main() -> int:
     parser.add_argument("--profile-kernel", choices=["attention", "elementwise"],
                         help="launch one kernel family for an ncu capture")
     parser.add_argument("--heads-per-rank", type=int, default=3)
+    parser.add_argument("--exchange-bench", action="store_true",
+                        help="N>1: time the exchange operations alone (peer stores vs NCCL)")
     args = parser.parse_args()
     sys.path.insert(0, str(ROOT))
     from h3_flash_b200.workloads import CONFIGS
 
     if args.profile_kernel:
         profile_kernel(args)
+        return 0
+    if args.exchange_bench:
+        line = exchange_bench(args)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
         return 0
     if args.sweep == "elementwise":
         print(json.dumps(elementwise_sweep(args)), flush=True)
