@@ -61,6 +61,8 @@ class PackedUlyssesRuntime:
     def begin_request(self) -> None:
         # Every rank calls this at the same request boundary; the next attention
         # call gathers the (possibly uneven) shard sizes collectively, once.
+        if self.peer is not None:
+            self.peer.check()
         self._row_counts = None
         self.requests += 1
 

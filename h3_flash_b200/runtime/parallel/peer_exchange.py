@@ -162,6 +162,18 @@ class PeerExchange:
              ptr(q_weight.contiguous()), ptr(k_weight.contiguous()), ptr(cos32), ptr(sin32), rows,
              heads, head_dim, rotary_dim, float(q_eps), float(k_eps), stream_of(q))
 
+    def check(self) -> None:
+        """Raise if a barrier of an earlier call gave up on a peer (status bit 2,
+        set after 10 s): the rows it exchanged are incomplete. Reads the device
+        status word (a host sync), so call it at request boundaries."""
+
+        if _lib.device_status() & 2:
+            _lib.clear_device_status(torch.cuda.current_stream(self.device).cuda_stream)
+            raise RuntimeError(
+                "packed Ulysses peer exchange: a peer did not reach the exchange barrier "
+                "within 10 s; the previous request's outputs are invalid"
+            )
+
     def barrier(self) -> None:
         call("h3b_peer_barrier", self._flag_ptrs, self.world, self.rank,
              torch.cuda.current_stream(self.device).cuda_stream)
