@@ -346,7 +346,8 @@ def run_h3b(args) -> dict | None:
     if world > 1:
         from h3_flash_b200.runtime.parallel import install_packed_ulysses
 
-        runtime = install_packed_ulysses(stack, exchange=args.exchange)
+        runtime = install_packed_ulysses(stack, exchange=args.exchange,
+                                         fuse_output_exchange=args.output_exchange == "fused")
         runtime.begin_request()
     start, stop = split_bounds(cfg.seq, world, rank)
     rows = stop - start
@@ -440,10 +441,14 @@ def run_h3b(args) -> dict | None:
     ew_ms = _max_over_ranks(ew_ms, world)
     a2a_bytes = (4 * r * d * 2) * (world - 1) / world if world > 1 else 0.0
     a2a_ms = _max_over_ranks(sum(sections.get("all_to_all", [0.0])) / max(args.steps, 1), world)
+    fused_output = world > 1 and args.exchange == "p2p" and args.output_exchange == "fused"
     if world > 1 and args.exchange == "p2p":
         # the QKV exchange happens inside the pack kernel: count the whole pack
         a2a_ms = _max_over_ranks(sum(sections.get("all_to_all", [0.0]) + sections.get("qknorm_rope_pack", [0.0]))
                                  / max(args.steps, 1), world)
+    if fused_output:
+        # the output rows leave inside the attention kernel, whose time is the attention's
+        a2a_bytes = (3 * r * d * 2) * (world - 1) / world
     sections_total = {k: round(sum(v) / args.steps, 4) for k, v in sections.items()}
 
     if rank != 0:
@@ -467,7 +472,8 @@ def run_h3b(args) -> dict | None:
             "dim": cfg.dim, "heads": cfg.heads, "head_dim": cfg.head_dim, "ffn": f"{cfg.ffn_inner} gelu-tanh",
             "rotary_dim": cfg.rotary_dim, "rows_per_rank": rows, "heads_per_rank": hl,
             "parallelism": f"ulysses_sp{world}",
-            "exchange": (args.exchange if world > 1 else "none"), "l2": "flushed between timed steps (256 MiB write, then read back)",
+            "exchange": (args.exchange + (" (output exchange in the attention epilogue)" if fused_output else "")
+                         if world > 1 else "none"), "l2": "flushed between timed steps (256 MiB write, then read back)",
         },
         "e2e": {"value": round(e2e_pipelined, 4), "unit": "ms",
                 "h2d_bytes_per_step": hidden_host.numel() * hidden_host.element_size(),
@@ -480,7 +486,8 @@ def run_h3b(args) -> dict | None:
         "e2e_serial": {"value": round(e2e_mean, 4), "unit": "ms",
                        "mode": "each step alone: H2D, block, D2H back to back on one stream"},
         "roofline": {
-            "kernel": "h3b attention_fwd (tcgen05)",
+            "kernel": "h3b attention_fwd (tcgen05)" + (", output rows stored at their owners over NVLink"
+                                                     if fused_output else ""),
             "bound": "tensor",
             "achieved": round(achieved, 2),
             "peak": peak,
@@ -503,6 +510,9 @@ def run_h3b(args) -> dict | None:
                                   "achieved_gbs": round(a2a_bytes / (a2a_ms * 1e-3) / 1e9, 1) if a2a_ms else None,
                                   "peak_gbs": NVLINK_PEER_GBS, "nominal_gbs": 900.0,
                                   "peak_note": "measured peer copy per direction on this pool",
+                                  "covers": ("QKV rows (pack kernel + barriers); the output rows move "
+                                             "inside the attention kernel" if fused_output
+                                             else "QKV and output rows"),
                                   "frac": round(a2a_bytes / (a2a_ms * 1e-3) / 1e9 / NVLINK_PEER_GBS, 4)
                                   if a2a_ms else None},
         },
@@ -706,6 +716,9 @@ def main() -> int:
     parser.add_argument("--warmup", type=int, default=3)
     parser.add_argument("--impl", choices=["h3b", "reference"], default="h3b")
     parser.add_argument("--config", default="480p-5s")
+    parser.add_argument("--output-exchange", choices=["fused", "scatter"], default="fused",
+                        help="p2p: attention stores its output rows at their owners (fused) or a "
+                             "scatter kernel moves them after attention")
     parser.add_argument("--exchange", choices=["nccl", "p2p"], default="p2p",
                         help="packed-Ulysses row exchange for N>1: NCCL all-to-all or NVLink peer stores")
     parser.add_argument("--no-cpu-baseline", action="store_true")

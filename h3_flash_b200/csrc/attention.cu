@@ -30,6 +30,13 @@
 // commit after S_t(j) also certifies that PV_t(j-1) is done: the softmax may
 // touch O_t once it has seen S_t(j).
 //
+// Output: the local [B, S, H, D] tensor, or (h3b_attention_p2p) the merged
+// buffers of the ranks that own the rows. There the epilogue stores each
+// finished row of local head h over NVLink into its owner's [rows, H, D] buffer
+// at head rank*hl + h: the output all-to-all and the head merge of packed
+// Ulysses run inside the attention kernel, tile by tile, while later tiles
+// are still computing.
+//
 // Every mbarrier wait is bounded by a wall-clock limit. On expiry the thread
 // ORs kStatusAttentionTimeout into the library status word, raises the CTA
 // abort flag and unwinds; the other roles see the flag in their own waits, so
@@ -42,6 +49,7 @@
 
 #include <cmath>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -385,9 +393,19 @@ __device__ __forceinline__ float2 exp2_poly(float2 x) {
 // Kernel
 // ---------------------------------------------------------------------------
 
+// Where output rows go when they leave this rank: the merged buffer
+// dst[o] = [rows_o, heads_total, D] of the rank o that owns global row s
+// (start[o] <= s < start[o+1]), at head head_base + h. world == 0: local out.
+struct OutRoute {
+  PeerPtrs dst;
+  int64_t start[kMaxPeers + 1];
+  int world, head_base, heads_total;
+};
+
 struct Params {
   __nv_bfloat16* out;
   int64_t o_batch_stride, o_row_stride, o_head_stride;
+  OutRoute route;
   int seq_q, seq_k;
   float scale_log2;  // softmax_scale * log2(e)
   unsigned int* status;
@@ -398,6 +416,22 @@ struct Params {
   int heads, units_per_bh, n_full, splits, blocks_per_split;
   float* ws;
 };
+
+// First element of output row `row`, head `head`.
+__device__ __forceinline__ __nv_bfloat16* out_row(const Params& prm, int batch, int row,
+                                                  int head) {
+  if (prm.route.world == 0)
+    return prm.out + (int64_t)batch * prm.o_batch_stride + (int64_t)row * prm.o_row_stride +
+           (int64_t)head * prm.o_head_stride;
+  // Owner = last rank whose first row is <= row (starts never decrease).
+  int owner = 0;
+  int64_t first = 0;
+#pragma unroll
+  for (int j = 1; j < kMaxPeers; ++j)
+    if (j < prm.route.world && row >= prm.route.start[j]) owner = j, first = prm.route.start[j];
+  return reinterpret_cast<__nv_bfloat16*>(peer_at(prm.route.dst, owner)) +
+         ((row - first) * prm.route.heads_total + prm.route.head_base + head) * kHeadDim;
+}
 
 // Workspace floats per split CTA: per tile, O [128 x 128] then (m, l) [128 x 2].
 constexpr int kWsTileFloats = kBlockM * kHeadDim + 2 * kBlockM;
@@ -720,8 +754,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       float* ws = split_slot >= 0
                       ? prm.ws + (int64_t)split_slot * kWsSlotFloats + t * kWsTileFloats
                       : nullptr;
-      __nv_bfloat16* dst = prm.out + (int64_t)batch * prm.o_batch_stride +
-                           (int64_t)row * prm.o_row_stride + (int64_t)head * prm.o_head_stride;
+      __nv_bfloat16* dst =
+          (ws == nullptr && row < prm.seq_q) ? out_row(prm, batch, row, head) : nullptr;
 #pragma unroll 1
       for (int q4 = 0; q4 < 4; ++q4) {
         uint32_t o[32];
@@ -755,6 +789,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         float* ml = ws + kBlockM * kHeadDim + 2 * row_in_tile;
         ml[0] = m_use;
         ml[1] = l_sum;
+      } else if (prm.route.world != 0) {
+        __threadfence_system();
       }
     }
   }
@@ -807,13 +843,12 @@ __global__ void __launch_bounds__(256) attention_combine(const Params prm, int s
     acc.w += scale * o.w;
   }
   const float inv = 1.f / l_tot;
-  __nv_bfloat16* dst = prm.out + (int64_t)batch * prm.o_batch_stride +
-                       (int64_t)row * prm.o_row_stride + (int64_t)head * prm.o_head_stride +
-                       lane * 4;
+  __nv_bfloat16* dst = out_row(prm, batch, row, head) + lane * 4;
   uint2 u;
   u.x = pack_bf16(acc.x * inv, acc.y * inv);
   u.y = pack_bf16(acc.z * inv, acc.w * inv);
   *reinterpret_cast<uint2*>(dst) = u;
+  if (prm.route.world != 0) __threadfence_system();
 }
 
 // Work plan of one call: which units run whole and how the last, partial wave
@@ -905,15 +940,17 @@ int make_map(CUtensorMap* map, const void* base, int64_t batch, int64_t seq, int
 }  // namespace attn
 }  // namespace h3b
 
-extern "C" int h3b_attention(void* out, const void* q, const void* k, const void* v,
-                             int64_t batch, int64_t seq_q, int64_t seq_k, int64_t heads,
-                             int64_t head_dim, int64_t q_batch_stride, int64_t q_row_stride,
-                             int64_t q_head_stride, int64_t k_batch_stride,
-                             int64_t k_row_stride, int64_t k_head_stride,
-                             int64_t v_batch_stride, int64_t v_row_stride,
-                             int64_t v_head_stride, int64_t o_batch_stride,
-                             int64_t o_row_stride, int64_t o_head_stride, float softmax_scale,
-                             void* workspace, int64_t workspace_bytes, h3b_stream_t stream) {
+namespace {
+
+// h3b_attention with an optional output route (nullptr: the local `out`).
+int attention_launch(void* out, const void* q, const void* k, const void* v, int64_t batch,
+                     int64_t seq_q, int64_t seq_k, int64_t heads, int64_t head_dim,
+                     int64_t q_batch_stride, int64_t q_row_stride, int64_t q_head_stride,
+                     int64_t k_batch_stride, int64_t k_row_stride, int64_t k_head_stride,
+                     int64_t v_batch_stride, int64_t v_row_stride, int64_t v_head_stride,
+                     int64_t o_batch_stride, int64_t o_row_stride, int64_t o_head_stride,
+                     float softmax_scale, void* workspace, int64_t workspace_bytes,
+                     const h3b::attn::OutRoute* route, h3b_stream_t stream) {
   using namespace h3b::attn;
   H3B_REQUIRE(batch >= 0 && seq_q >= 0 && seq_k >= 0 && heads >= 0,
               "attention: negative shape");
@@ -927,12 +964,12 @@ extern "C" int h3b_attention(void* out, const void* q, const void* k, const void
                   ((seq_q + 255) / 256) * heads * batch < (1LL << 31),
               "attention: shape exceeds launch limits");
   H3B_REQUIRE(h3b::aligned16(q) && h3b::aligned16(k) && h3b::aligned16(v) &&
-                  h3b::aligned16(out),
+                  (route != nullptr || h3b::aligned16(out)),
               "attention: q, k, v, out must be 16-byte aligned");
   const int64_t strides[12] = {q_batch_stride, q_row_stride, q_head_stride, k_batch_stride,
                                k_row_stride,   k_head_stride, v_batch_stride, v_row_stride,
                                v_head_stride,  o_batch_stride, o_row_stride, o_head_stride};
-  for (int i = 0; i < 12; ++i) {
+  for (int i = 0; i < (route != nullptr ? 9 : 12); ++i) {
     const bool unit = (i % 3 == 0 && batch == 1) || (i % 3 == 2 && heads == 1);
     H3B_REQUIRE(unit || (strides[i] % 8 == 0 && strides[i] > 0),
                 "attention: strides must be positive multiples of 8 elements");
@@ -978,6 +1015,11 @@ extern "C" int h3b_attention(void* out, const void* q, const void* k, const void
   p.o_batch_stride = o_batch_stride;
   p.o_row_stride = o_row_stride;
   p.o_head_stride = o_head_stride;
+  if (route != nullptr) {
+    p.route = *route;
+  } else {
+    memset(&p.route, 0, sizeof(p.route));
+  }
   p.seq_q = (int)seq_q;
   p.seq_k = (int)seq_k;
   p.scale_log2 = (float)((double)softmax_scale * 1.4426950408889634);
@@ -996,6 +1038,66 @@ extern "C" int h3b_attention(void* out, const void* q, const void* k, const void
     attention_combine<<<(unsigned)((warps + 7) / 8), 256, 0, stream>>>(p, pl.split_units);
   }
   return h3b::check_launch("h3b_attention");
+}
+
+}  // namespace
+
+extern "C" int h3b_attention(void* out, const void* q, const void* k, const void* v,
+                             int64_t batch, int64_t seq_q, int64_t seq_k, int64_t heads,
+                             int64_t head_dim, int64_t q_batch_stride, int64_t q_row_stride,
+                             int64_t q_head_stride, int64_t k_batch_stride,
+                             int64_t k_row_stride, int64_t k_head_stride,
+                             int64_t v_batch_stride, int64_t v_row_stride,
+                             int64_t v_head_stride, int64_t o_batch_stride,
+                             int64_t o_row_stride, int64_t o_head_stride, float softmax_scale,
+                             void* workspace, int64_t workspace_bytes, h3b_stream_t stream) {
+  return attention_launch(out, q, k, v, batch, seq_q, seq_k, heads, head_dim, q_batch_stride,
+                          q_row_stride, q_head_stride, k_batch_stride, k_row_stride,
+                          k_head_stride, v_batch_stride, v_row_stride, v_head_stride,
+                          o_batch_stride, o_row_stride, o_head_stride, softmax_scale, workspace,
+                          workspace_bytes, nullptr, stream);
+}
+
+extern "C" int h3b_attention_p2p(void* const* merged_ptrs, const int64_t* row_counts,
+                                 int64_t world, int64_t rank, const void* qkv,
+                                 int64_t heads_local, int64_t head_dim, float softmax_scale,
+                                 void* workspace, int64_t workspace_bytes,
+                                 h3b_stream_t stream) {
+  using namespace h3b::attn;
+  using h3b::kMaxPeers;
+  H3B_REQUIRE(world >= 1 && world <= kMaxPeers, "attention_p2p: world size must be 1..%d",
+              kMaxPeers);
+  H3B_REQUIRE(rank >= 0 && rank < world, "attention_p2p: rank %lld outside world %lld",
+              (long long)rank, (long long)world);
+  H3B_REQUIRE(merged_ptrs != nullptr && row_counts != nullptr && qkv != nullptr,
+              "attention_p2p: null argument");
+  H3B_REQUIRE(heads_local > 0 && heads_local * world <= (1LL << 20),
+              "attention_p2p: heads_local must be positive");
+  if (head_dim != kHeadDim) {
+    h3b::set_error("h3b_attention_p2p: head_dim must be 128");
+    return H3B_ERR_UNSUPPORTED;
+  }
+  OutRoute route;
+  memset(&route, 0, sizeof(route));
+  for (int i = 0; i < world; ++i) {
+    H3B_REQUIRE(row_counts[i] >= 0, "attention_p2p: negative row count");
+    H3B_REQUIRE(merged_ptrs[i] != nullptr && h3b::aligned16(merged_ptrs[i]),
+                "attention_p2p: merged buffer of rank %d is null or not 16-byte aligned", i);
+    route.dst.p[i] = merged_ptrs[i];
+    route.start[i + 1] = route.start[i] + row_counts[i];
+  }
+  for (int i = (int)world + 1; i <= kMaxPeers; ++i) route.start[i] = route.start[world];
+  route.world = (int)world;
+  route.head_base = (int)(rank * heads_local);
+  route.heads_total = (int)(heads_local * world);
+  const int64_t seq = route.start[world];
+  if (seq == 0) return H3B_OK;
+  // The packed receive buffer [S, hl, 3D]: q | k | v per head.
+  const auto* base = static_cast<const __nv_bfloat16*>(qkv);
+  const int64_t rs = heads_local * 3 * kHeadDim, hs = 3 * kHeadDim;
+  return attention_launch(nullptr, base, base + kHeadDim, base + 2 * kHeadDim, 1, seq, seq,
+                          heads_local, head_dim, 0, rs, hs, 0, rs, hs, 0, rs, hs, 0, 0, 0,
+                          softmax_scale, workspace, workspace_bytes, &route, stream);
 }
 
 extern "C" int h3b_attention_workspace_size(int64_t batch, int64_t seq_q, int64_t seq_k,

@@ -16,8 +16,9 @@ are fused into one kernel. Row counts are exchanged once per request.
 
 With ``exchange="p2p"`` the two NCCL all-to-alls, the send buffer and the
 merge are replaced by peer stores over NVLink (peer_exchange.py): the pack
-kernel writes each head row into its owner's receive buffer and a scatter
-kernel writes each output row into its owner's merged buffer.
+kernel writes each head row into its owner's receive buffer and the attention
+kernel's epilogue writes each output row into its owner's merged buffer
+(``fuse_output_exchange=False``: a separate scatter kernel after attention).
 """
 
 from __future__ import annotations
@@ -39,9 +40,10 @@ from .relayout import can_pack_qkv, merge_heads, pack_qkv_destination_major
 class PackedUlyssesRuntime:
     """Request-scoped shape metadata and auditable counters (packed_ulysses.py:19-64)."""
 
-    def __init__(self, group: Any, exchange: str = "nccl") -> None:
+    def __init__(self, group: Any, exchange: str = "nccl", fuse_output_exchange: bool = True) -> None:
         if exchange not in ("nccl", "p2p"):
             raise ValueError(f"exchange must be 'nccl' or 'p2p', got {exchange!r}")
+        self.fuse_output_exchange = fuse_output_exchange
         self.group = group
         self.world = dist.get_world_size(group)
         self._row_counts: tuple[list[int], int] | None = None
@@ -272,7 +274,9 @@ def _p2p_supported(head_dim: int, cos: Any) -> bool:
 
 def _peer_attention(runtime: PackedUlyssesRuntime, q, k, v, norm_q, norm_k, cos, sin,
                     rows_local: int, head_dim: int) -> torch.Tensor:
-    """pack_p2p -> barrier -> attention -> scatter_p2p -> barrier. Returns [r, H, D]."""
+    """pack_p2p -> barrier -> attention_p2p (output exchange in its epilogue) ->
+    barrier, or with ``fuse_output_exchange=False`` attention -> scatter_p2p in
+    place of attention_p2p. Returns [r, H, D]."""
 
     peer = runtime.peer
     counts = runtime.row_counts(rows_local)
@@ -281,6 +285,12 @@ def _peer_attention(runtime: PackedUlyssesRuntime, q, k, v, norm_q, norm_k, cos,
     with TIMER.section("all_to_all"):
         peer.barrier()
     heads_local = q.shape[1] // runtime.world
+    if runtime.fuse_output_exchange:
+        with TIMER.section("attention"):
+            merged = peer.attention(counts, heads_local, head_dim)
+        with TIMER.section("all_to_all"):
+            peer.barrier()
+        return merged
     with TIMER.section("attention"):
         output = packed_attention(peer.recv_view(sum(counts), heads_local, head_dim), head_dim)
     with TIMER.section("all_to_all"):
@@ -300,19 +310,21 @@ def _single_node_cuda_group(group: Any) -> bool:
 
 
 def install_packed_ulysses(transformer: Any, *, group: Any = None, fused_qknorm_rope: bool = True,
-                           exchange: str = "auto") -> PackedUlyssesRuntime:
+                           exchange: str = "auto", fuse_output_exchange: bool = True) -> PackedUlyssesRuntime:
     """Replace each block's attention forward with the packed-Ulysses path (packed_ulysses.py:131-220).
 
     ``exchange``: ``"p2p"`` moves rows with peer stores over NVLink (one process
     per GPU on one node, CUDA IPC available), ``"nccl"`` with NCCL all-to-alls;
-    ``"auto"`` (collective) picks p2p when all ranks are NCCL ranks on one host."""
+    ``"auto"`` (collective) picks p2p when all ranks are NCCL ranks on one host.
+    ``fuse_output_exchange`` (p2p only): the attention kernel stores its output rows
+    into the owners' merged buffers itself, instead of a scatter kernel after it."""
 
     if not (dist.is_available() and dist.is_initialized()):
         raise RuntimeError("packed Ulysses requires an initialized process group")
     group = group or dist.group.WORLD
     if exchange == "auto":
         exchange = "p2p" if _single_node_cuda_group(group) else "nccl"
-    runtime = PackedUlyssesRuntime(group, exchange=exchange)
+    runtime = PackedUlyssesRuntime(group, exchange=exchange, fuse_output_exchange=fuse_output_exchange)
     if runtime.world < 2:
         raise RuntimeError("packed Ulysses degree must be at least two")
 

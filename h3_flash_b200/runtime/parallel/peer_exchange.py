@@ -10,10 +10,14 @@ Then, per attention call, on the current stream:
   h3b_qknorm_rope_pack_p2p   QK-norm + RoPE, each head row stored straight into
                              the owning rank's receive buffer [S, hl, 3D]
   h3b_peer_barrier           all peers' rows have landed
-  packed attention           on the own receive buffer
-  h3b_scatter_heads_p2p      each output row stored into its owner's merged
-                             buffer [r, H, D] (exchange + merge_heads in one pass)
+  h3b_attention_p2p          attention on the own receive buffer; its epilogue
+                             stores each output row into its owner's merged
+                             buffer [r, H, D] (exchange + merge_heads inside the
+                             attention kernel)
   h3b_peer_barrier           all peers' output rows have landed
+
+``scatter`` is the unfused form of the third step: attention into a local
+[S, hl, D] tensor, then h3b_scatter_heads_p2p moves its rows (same bits).
 
 The result is a view of the merged buffer; the next call on this runtime
 overwrites it, after the first barrier, so it must be consumed (the output
@@ -24,6 +28,7 @@ request's row counts and regrown collectively when a larger request arrives.
 from __future__ import annotations
 
 import ctypes
+import math
 from typing import Any
 
 import torch
@@ -177,6 +182,27 @@ class PeerExchange:
     def barrier(self) -> None:
         call("h3b_peer_barrier", self._flag_ptrs, self.world, self.rank,
              torch.cuda.current_stream(self.device).cuda_stream)
+
+    def attention(self, counts: list[int], heads_local: int, head_dim: int,
+                  softmax_scale: float | None = None) -> torch.Tensor:
+        """Attention over this rank's receive buffer with the output exchange and
+        head merge fused into its epilogue. Returns this rank's merged rows (a
+        view of its buffer), complete after the next ``barrier``."""
+
+        from ..attention.dense import workspace_bytes
+
+        total = sum(counts)
+        if self._buffer is None or total * heads_local * 3 * head_dim * 2 > self._recv_bytes \
+                or max(counts) * heads_local * self.world * head_dim * 2 > self._merged_bytes:
+            raise RuntimeError("attention before pack: the exchange buffers are not sized for this request")
+        scale = float(softmax_scale) if softmax_scale is not None else 1.0 / math.sqrt(head_dim)
+        ws_bytes = workspace_bytes(1, total, total, heads_local, head_dim)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=self.device) if ws_bytes else None
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        call("h3b_attention_p2p", self._merged_ptrs, self._counts(counts), self.world, self.rank,
+             ptr(self._buffer), heads_local, head_dim, scale, ptr(ws) if ws is not None else None,
+             ws_bytes, stream)
+        return self.merged_view(counts[self.rank], heads_local * self.world, head_dim)
 
     def scatter(self, output: torch.Tensor, counts: list[int]) -> torch.Tensor:
         """Output exchange + head merge: [S, hl, D] of this rank's heads -> every owner's

@@ -30,7 +30,7 @@ typedef struct CUstream_st* h3b_stream_t; /* == cudaStream_t */
 #define H3B_ERR_CUDA 2        /* CUDA launch or driver error: RuntimeError         */
 #define H3B_ERR_UNSUPPORTED 3 /* valid input this build does not handle: RuntimeError */
 
-#define H3B_ABI_VERSION 3
+#define H3B_ABI_VERSION 4
 
 int h3b_abi_version(void);
 /* Message of the last failing call on this host thread ("" if none). */
@@ -201,11 +201,12 @@ int h3b_attention_noalloc(void* out, const void* q, const void* k, const void* v
  * host arrays of `world` device pointers indexed by rank, this rank's own
  * local pointer included; world <= 16. One attention call on every rank runs,
  * on one stream:
- *   h3b_qknorm_rope_pack_p2p -> h3b_peer_barrier -> h3b_attention on the own
- *   receive buffer -> h3b_scatter_heads_p2p -> h3b_peer_barrier
- * and then reads its merged buffer. With that order single buffers are safe
- * across consecutive calls. All ranks must make the same calls in the same
- * order.
+ *   h3b_qknorm_rope_pack_p2p -> h3b_peer_barrier -> h3b_attention_p2p on the
+ *   own receive buffer -> h3b_peer_barrier
+ * (or, unfused, h3b_attention then h3b_scatter_heads_p2p in place of
+ * h3b_attention_p2p) and then reads its merged buffer. With that order single
+ * buffers are safe across consecutive calls. All ranks must make the same
+ * calls in the same order.
  * ------------------------------------------------------------------------- */
 
 /* h3b_qknorm_rope_pack with the pack's store going straight to the owner of
@@ -232,6 +233,20 @@ int h3b_qknorm_rope_pack_p2p(void* const* recv_ptrs, int64_t world, int64_t row_
 int h3b_scatter_heads_p2p(void* const* merged_ptrs, const int64_t* row_counts, const void* out,
                           int64_t world, int64_t rank, int64_t heads_local, int64_t head_dim,
                           h3b_stream_t stream);
+
+/* Attention over this rank's receive buffer qkv = [S_total, heads_local,
+ * 3*head_dim] (S_total = sum of row_counts) whose epilogue stores every output
+ * row straight into its owner's merged buffer, at the same place
+ * h3b_scatter_heads_p2p would put it: the output exchange runs inside the
+ * attention kernel, overlapped with the tiles still computing. Results are
+ * bit-identical to h3b_attention followed by h3b_scatter_heads_p2p. workspace
+ * as for h3b_attention with batch 1, seq_q = seq_k = S_total, heads_local heads.
+ * replaces the SDPA call and _packed_output_all_to_all
+ *          packed_ulysses.py:201-209, :111-128 (merge_heads relayout.py:133-159) */
+int h3b_attention_p2p(void* const* merged_ptrs, const int64_t* row_counts, int64_t world,
+                      int64_t rank, const void* qkv, int64_t heads_local, int64_t head_dim,
+                      float softmax_scale, void* workspace, int64_t workspace_bytes,
+                      h3b_stream_t stream);
 
 /* Cross-rank barrier on the ranks' flag arrays; orders every earlier store of
  * this stream before every later load of the peers' streams. The epoch lives

@@ -66,3 +66,19 @@ def test_empty_inputs_are_noops():
     _lib.call("h3b_swiglu", None, None, 0, 16, 32, 16, None)
     _lib.call("h3b_merge_heads", None, None, 2, 0, 128, None)
     _lib.call("h3b_attention", None, None, None, None, 1, 0, 5, 1, 128, *([128] * 12), 1.0, None, 0, None)
+
+
+def test_attention_p2p_argument_errors_without_a_gpu():
+    """Validation returns before any CUDA call; the pointers are never dereferenced."""
+
+    fake = 1 << 20  # a 16-byte aligned address
+    ptrs = (ctypes.c_void_p * 2)(fake, None)
+    counts = (ctypes.c_int64 * 2)(4, 4)
+    with pytest.raises(ValueError, match="merged buffer of rank 1"):
+        _lib.call("h3b_attention_p2p", ptrs, counts, 2, 0, fake, 1, 128, 0.1, None, 0, None)
+    with pytest.raises(ValueError, match="rank 2 outside"):
+        _lib.call("h3b_attention_p2p", ptrs, counts, 2, 2, fake, 1, 128, 0.1, None, 0, None)
+    with pytest.raises(ValueError, match="world size"):
+        _lib.call("h3b_attention_p2p", ptrs, counts, 17, 0, fake, 1, 128, 0.1, None, 0, None)
+    with pytest.raises(RuntimeError, match="head_dim must be 128"):
+        _lib.call("h3b_attention_p2p", ptrs, counts, 2, 0, fake, 1, 64, 0.1, None, 0, None)

@@ -4,7 +4,12 @@ The peer path must reproduce the NCCL path bit for bit:
 - the receive buffer after pack_p2p + barrier equals fused_qknorm_rope_pack +
   all_to_all_single;
 - the merged buffer after scatter_p2p + barrier equals all_to_all_single + merge_heads;
-- a block stack run with exchange="p2p" equals the same stack run over NCCL.
+- the merged buffer after attention_p2p (output exchange in the attention epilogue)
+  + barrier equals attention + all_to_all_single + merge_heads;
+- a block stack run with exchange="p2p" (fused output exchange) equals the same stack
+  run over NCCL.
+Single-GPU: attention_p2p routes every row of every 'rank' to the right owner and head
+slot, bit-identical to the local attention output (all 'peers' are local buffers).
 This holds over several requests of different (uneven) row splits, so the buffers are
 reused and regrown, and for one request in which a rank holds no rows. One single-GPU
 test makes the barrier's bounded wait run out on a flag that nothing sets, and checks
@@ -40,6 +45,7 @@ def _worker(rank, world, port, queue):
         dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
                                 timeout=datetime.timedelta(seconds=60), device_id=torch.device("cuda", rank))
         from h3_flash_b200 import _lib
+        from h3_flash_b200.runtime.attention.dense import packed_attention
         from h3_flash_b200.runtime.h3_block import H3BlockStack, H3TransformerBlock
         from h3_flash_b200.runtime.kernels import install_transformer_fusions
         from h3_flash_b200.runtime.kernels.fusions import fused_qknorm_rope_pack
@@ -82,6 +88,12 @@ def _worker(rank, world, port, queue):
             got_back = peer.scatter(out, counts)
             peer.barrier()
             checks[f"out_{request}"] = bool(torch.equal(got_back, want_back))
+            # attention with the output exchange in its epilogue vs attention + NCCL + merge
+            want_merged = _packed_output_all_to_all(packed_attention(want, 128), rows, nccl_rt)
+            peer.barrier()  # the pack's barrier of a call: peers are done reading their merged rows
+            got_merged = peer.attention(counts, heads // world, 128)
+            peer.barrier()
+            checks[f"attn_{request}"] = bool(torch.equal(got_merged, want_merged))
         checks["regrown"] = p2p_rt.peer.reallocations == 2  # the third request fits
 
         # 2) a two-block stack, NCCL vs p2p, two requests of different splits
@@ -171,3 +183,42 @@ def test_peer_barrier_gives_up_on_a_missing_peer():
         _lib.clear_device_status(stream)
         torch.cuda.synchronize()
     assert _lib.device_status() == 0
+
+
+@pytest.mark.parametrize("seq,heads_local,counts", [
+    (333, 3, [100, 0, 233]),          # split tail (combine kernel), a rank with no rows
+    (4096, 2, [1000, 3096]),          # split tail
+    (37888, 1, [18944, 18944]),       # 148 whole units: no split
+])
+def test_attention_p2p_routes_rows_to_owners(seq, heads_local, counts):
+    """Every 'rank' r of a world whose merged buffers all live on this GPU: row s of local
+    head h must land in owner o's buffer at (s - start_o, r*hl + h), bit-identical to the
+    plain attention output (the buffers start as NaN, so a slot nobody wrote fails)."""
+
+    from h3_flash_b200 import _lib
+    from h3_flash_b200.runtime.attention.dense import packed_attention, workspace_bytes
+
+    world = len(counts)
+    g = torch.Generator(device="cuda").manual_seed(seq)
+    packed = torch.randn(seq, heads_local, 384, device="cuda", generator=g).to(torch.bfloat16)
+    want = packed_attention(packed, 128)
+    heads = world * heads_local
+    merged = [torch.full((max(c, 1), heads, 128), float("nan"), dtype=torch.bfloat16, device="cuda")
+              for c in counts]
+    ptrs = (ctypes.c_void_p * world)(*[m.data_ptr() for m in merged])
+    arr = (ctypes.c_int64 * world)(*counts)
+    ws_bytes = workspace_bytes(1, seq, seq, heads_local)
+    ws = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    for rank in range(world):
+        _lib.call("h3b_attention_p2p", ptrs, arr, world, rank, packed.data_ptr(), heads_local, 128,
+                  1.0 / 128 ** 0.5, ws.data_ptr(), ws_bytes, stream)
+    torch.cuda.synchronize()
+    start = 0
+    for owner, c in enumerate(counts):
+        got = merged[owner][:c].view(c, world, heads_local, 128)
+        expect = want[start : start + c].unsqueeze(1).expand(c, world, heads_local, 128)
+        assert torch.equal(got, expect), owner
+        start += c
+    assert _lib.device_status() == 0
+
