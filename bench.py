@@ -341,14 +341,6 @@ def run_h3b(args) -> dict | None:
                                            qk_eps=cfg.eps), seed=0)
     block = block.to(device="cuda", dtype=torch.bfloat16).eval()
     stack = H3BlockStack([block])
-    install_transformer_fusions(stack)
-    runtime = None
-    if world > 1:
-        from h3_flash_b200.runtime.parallel import install_packed_ulysses
-
-        runtime = install_packed_ulysses(stack, exchange=args.exchange,
-                                         fuse_output_exchange=args.output_exchange == "fused")
-        runtime.begin_request()
     start, stop = split_bounds(cfg.seq, world, rank)
     rows = stop - start
     g = torch.Generator().manual_seed(1 + start)
@@ -360,6 +352,28 @@ def run_h3b(args) -> dict | None:
     out_host = torch.empty_like(hidden_host).pin_memory()
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     stream = torch.cuda.current_stream()
+
+    # The same block before any of this package's kernels are installed: torch ops,
+    # torch SDPA and cuBLAS (one GPU only; the reference's own Triton kernels do not
+    # run without its source tree).
+    eager = None
+    if world == 1 and not args.no_eager_baseline:
+        with torch.no_grad():
+            eager_steps = min(args.steps, 5)
+            eager_ms = _timed(lambda: stack(hidden, None, idx, rotary), eager_steps, 3, flush)
+        eager = {"ms_per_step": round(eager_ms, 4), "steps": eager_steps, "warmup": 3,
+                 "what": "the same block unfused: torch RMSNorm/RoPE/modulate/GELU ops, torch SDPA "
+                         "attention, cuBLAS GEMMs; L2 flushed between steps"}
+        torch.cuda.empty_cache()
+
+    install_transformer_fusions(stack, gemm_epilogue=not args.no_gemm_epilogue)
+    runtime = None
+    if world > 1:
+        from h3_flash_b200.runtime.parallel import install_packed_ulysses
+
+        runtime = install_packed_ulysses(stack, exchange=args.exchange,
+                                         fuse_output_exchange=args.output_exchange == "fused")
+        runtime.begin_request()
 
     def step(x):
         with torch.no_grad():
@@ -434,7 +448,7 @@ def run_h3b(args) -> dict | None:
     d = cfg.dim
     ew_bytes = (2 * r * d * 2            # rmsnorm_modulate: read x, write
                 + 4 * r * d * 2          # residual+rmsnorm+modulate: 2 reads, 2 writes
-                + 2 * r * cfg.ffn_inner * 2  # GELU: read, write
+                + (2 * r * cfg.ffn_inner * 2 if args.no_gemm_epilogue else 0)  # GELU kernel: read, write
                 + 3 * r * d * 2          # gated residual: 2 reads, 1 write
                 + 2 * 3 * r * d * 2)     # qknorm+rope+pack: read qkv, write packed
     ew_ms = sum(sum(v) / args.steps for k, v in sections.items() if k in ("elementwise", "qknorm_rope_pack"))
@@ -469,7 +483,7 @@ def run_h3b(args) -> dict | None:
         "config": {
             "workload": f"{cfg.name} DiT block forward, packed Ulysses SP{world}",
             "seq": cfg.seq, "video_tokens": cfg.video_tokens, "audio_tokens": cfg.audio_tokens,
-            "dim": cfg.dim, "heads": cfg.heads, "head_dim": cfg.head_dim, "ffn": f"{cfg.ffn_inner} gelu-tanh",
+            "dim": cfg.dim, "heads": cfg.heads, "head_dim": cfg.head_dim, "ffn": f"{cfg.ffn_inner} gelu-tanh" + ("" if args.no_gemm_epilogue else " (in the GEMM epilogue)"),
             "rotary_dim": cfg.rotary_dim, "rows_per_rank": rows, "heads_per_rank": hl,
             "parallelism": f"ulysses_sp{world}",
             "exchange": (args.exchange + (" (output exchange in the attention epilogue)" if fused_output else "")
@@ -517,6 +531,7 @@ def run_h3b(args) -> dict | None:
                                   if a2a_ms else None},
         },
         "sections_ms_per_step": sections_total,
+        "gpu_eager_baseline": eager,
         "gpu_launches": launches,
         "clocks": clocks,
     }
@@ -722,6 +737,10 @@ def main() -> int:
     parser.add_argument("--exchange", choices=["nccl", "p2p"], default="p2p",
                         help="packed-Ulysses row exchange for N>1: NCCL all-to-all or NVLink peer stores")
     parser.add_argument("--no-cpu-baseline", action="store_true")
+    parser.add_argument("--no-gemm-epilogue", action="store_true",
+                        help="GELU as a separate h3b kernel instead of inside the FFN GEMM")
+    parser.add_argument("--no-eager-baseline", action="store_true",
+                        help="skip timing the unfused torch block at N=1")
     parser.add_argument("--sweep", choices=["elementwise"], help="print the config-2 kernel sweep instead")
     parser.add_argument("--profile-kernel", choices=["attention", "elementwise"],
                         help="launch one kernel family for an ncu capture")

@@ -71,12 +71,37 @@ def _eager_activation(kind: str, projected: torch.Tensor) -> torch.Tensor:
     return torch.nn.functional.gelu(projected, approximate="tanh")
 
 
-def feed_forward(ff: Any, normed: torch.Tensor, fuse_activation: bool, gate: dict | None = None) -> torch.Tensor:
+def _gelu_epilogue_supported(proj: Any, x: torch.Tensor) -> bool:
+    """cuBLASLt's bias+GELU(tanh) epilogue serves a 2-D bf16/fp16 CUDA GEMM with a bias."""
+
+    weight, bias = getattr(proj, "weight", None), getattr(proj, "bias", None)
+    return (hasattr(torch, "_addmm_activation") and x.is_cuda and bias is not None and weight is not None
+            and x.dtype in (torch.bfloat16, torch.float16) and weight.dtype == x.dtype
+            and bias.dtype == x.dtype and weight.is_contiguous() and bias.is_contiguous()
+            and x.stride(-1) == 1 and x.numel() > 0)
+
+
+def feed_forward(ff: Any, normed: torch.Tensor, fuse_activation: bool, gate: dict | None = None,
+                 gemm_epilogue: bool = False) -> torch.Tensor:
+    """``gemm_epilogue``: a GELU-tanh FFN runs its activation inside the projection GEMM
+    (cuBLASLt bias+GELU epilogue), so the [rows, inner] pre-activation is never stored
+    and the pre-activation is not rounded to bf16 before the GELU."""
+
     act_layer, _, output_projection = ff.net
     kind = _activation_kind(act_layer, output_projection) if fuse_activation else None
     if kind is None:
         with TIMER.section("gemm"):
             return ff(normed)
+    if kind == "gelu_tanh" and gemm_epilogue and _gelu_epilogue_supported(act_layer.proj, normed):
+        proj = act_layer.proj
+        with TIMER.section("gemm"):
+            flat = normed.reshape(-1, normed.shape[-1])
+            activated = torch._addmm_activation(proj.bias, flat, proj.weight.t(), use_gelu=True)
+            activated = activated.view(*normed.shape[:-1], proj.out_features)
+        if gate is not None and "gelu_tanh_epilogue" not in gate:
+            gate["gelu_tanh_epilogue"] = _error_metrics(activated, _eager_activation(kind, proj(normed)))
+        with TIMER.section("gemm"):
+            return output_projection(activated)
     with TIMER.section("gemm"):
         projected = act_layer.proj(normed)
     with TIMER.section("elementwise"):
@@ -89,7 +114,8 @@ def feed_forward(ff: Any, normed: torch.Tensor, fuse_activation: bool, gate: dic
 
 def fused_block_forward(block: Any, hidden_states: torch.Tensor, temb: Any, adaln_indices: torch.Tensor,
                         rotary_emb: Any, attention_mask: Any = None, *, modulate: bool = True,
-                        swiglu: bool = True, gate: dict | None = None) -> torch.Tensor:
+                        swiglu: bool = True, gate: dict | None = None,
+                        gemm_epilogue: bool = False) -> torch.Tensor:
     """The patched ``block.forward`` body (kernels/transformer.py:40-126)."""
 
     shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = block.adaln_proj(temb)
@@ -123,7 +149,7 @@ def fused_block_forward(block: Any, hidden_states: torch.Tensor, temb: Any, adal
         hidden_states = hidden_states + gate_msa.index_select(0, adaln_indices) * attention_output
         normed = block.norm2(hidden_states)
         normed = normed * (1.0 + scale_mlp.index_select(0, adaln_indices)) + shift_mlp.index_select(0, adaln_indices)
-    feed_forward_output = feed_forward(block.ff, normed, swiglu, gate)
+    feed_forward_output = feed_forward(block.ff, normed, swiglu, gate, gemm_epilogue)
     if modulate:
         with TIMER.section("elementwise"):
             return fused_gated_residual(hidden_states, feed_forward_output, gate_mlp, adaln_indices)
@@ -131,6 +157,7 @@ def fused_block_forward(block: Any, hidden_states: torch.Tensor, temb: Any, adal
 
 
 def _patch_blocks(transformer: Any, modulate: bool, swiglu: bool, runtime: dict[str, Any]) -> None:
+    gemm_epilogue = bool(runtime.get("gemm_epilogue", False))
     for block_index, block in enumerate(transformer.transformer_blocks):
 
         def forward(hidden_states, temb, adaln_indices, rotary_emb, attention_mask=None, *, block=block,
@@ -138,6 +165,7 @@ def _patch_blocks(transformer: Any, modulate: bool, swiglu: bool, runtime: dict[
             return fused_block_forward(
                 block, hidden_states, temb, adaln_indices, rotary_emb, attention_mask,
                 modulate=modulate, swiglu=swiglu, gate=runtime["gate"] if gate_this_block else None,
+                gemm_epilogue=gemm_epilogue,
             )
 
         block.forward = forward
@@ -159,9 +187,11 @@ def _patch_attention(transformer: Any, runtime: dict[str, Any]) -> None:
 
 
 def install_transformer_fusions(transformer: Any, *, modulate: bool = True, swiglu: bool = True,
-                                qknorm_rope: bool = True) -> dict[str, Any]:
+                                qknorm_rope: bool = True, gemm_epilogue: bool = True) -> dict[str, Any]:
     """kernels/transformer.py:207-228. ``swiglu`` toggles the fused FFN activation
-    (SwiGLU for H3, GELU-tanh for the BASELINE block)."""
+    (SwiGLU for H3, GELU-tanh for the BASELINE block). ``gemm_epilogue`` runs a
+    GELU-tanh activation inside the FFN projection GEMM (cuBLASLt epilogue) instead
+    of the h3b elementwise kernel after it; SwiGLU always uses the h3b kernel."""
 
     if not HAVE_CUDA_KERNELS:
         raise RuntimeError("H3 transformer fusions require the h3b CUDA extension (libh3b.so)")
@@ -170,6 +200,7 @@ def install_transformer_fusions(transformer: Any, *, modulate: bool = True, swig
         "modulate": modulate,
         "swiglu": swiglu,
         "qknorm_rope": qknorm_rope,
+        "gemm_epilogue": gemm_epilogue,
         "origin": "B200-native sm_100a kernels (h3b)",
         "gate": {},
     }

@@ -85,3 +85,39 @@ def test_block_is_deterministic_and_reuses_qkv_cache():
         block.attn.to_q.weight.mul_(0.5)
         c = stack(*args)
     assert not torch.equal(a, c)
+
+
+def test_gelu_in_the_gemm_epilogue_is_tanh_gelu():
+    """The FFN projection with GELU in its epilogue (cuBLASLt) vs the fp32 GELU-tanh of the
+    fp32 projection: within the bf16 bar, no worse than the unfused GEMM + h3b GELU, and
+    tanh-GELU rather than erf-GELU where the two differ by many bf16 spacings (x near -3)."""
+
+    from h3_flash_b200.runtime.h3_block import FeedForward
+    from h3_flash_b200.runtime.kernels.transformer import feed_forward
+
+    torch.manual_seed(5)
+    ff = FeedForward(512, 2048, "gelu-tanh").to("cuda", torch.bfloat16)
+    with torch.no_grad():
+        ff.net[0].proj.weight.normal_(0.0, 0.1)
+        ff.net[0].proj.bias.normal_(0.0, 0.5)
+        x = torch.randn(1, 700, 512, device="cuda").to(torch.bfloat16)
+        gate = {}
+        # the activation itself: the same epilogue call feed_forward makes
+        proj = ff.net[0].proj
+        fused = torch._addmm_activation(proj.bias, x[0], proj.weight.t(), use_gelu=True).float()
+        unfused = torch.nn.functional.gelu(proj(x[0]).float(), approximate="tanh").to(torch.bfloat16).float()
+        pre = x[0].float() @ proj.weight.float().t() + proj.bias.float()
+        tanh_ref = torch.nn.functional.gelu(pre, approximate="tanh")
+        erf_ref = torch.nn.functional.gelu(pre)
+        out = feed_forward(ff, x, True, gate, gemm_epilogue=True)
+        out_unfused = feed_forward(ff, x, True, None, gemm_epilogue=False)
+    half_ulp = tanh_ref.abs().clamp_min(2.0 ** -126) * 2.0 ** -9
+    assert float(((fused - tanh_ref).abs() - half_ulp).max()) <= 2e-2
+    assert float((fused - tanh_ref).abs().mean()) <= float((unfused - tanh_ref).abs().mean()) * 1.05
+    distinct = (tanh_ref - erf_ref).abs() > 16 * half_ulp
+    assert int(distinct.sum()) > 100
+    closer = (fused - tanh_ref).abs()[distinct] < (fused - erf_ref).abs()[distinct]
+    assert float(closer.float().mean()) > 0.99
+    assert gate["gelu_tanh_epilogue"]["cosine"] > 0.9999
+    cos = torch.nn.functional.cosine_similarity(out.float().flatten(), out_unfused.float().flatten(), dim=0)
+    assert float(cos) > 0.9999
