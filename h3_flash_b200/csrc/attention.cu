@@ -16,9 +16,9 @@
 //               row: it loads the row's 128 scores of a block from TMEM, takes
 //               the row max itself (no exchange between threads), computes
 //               p = 2^(s*c - m), writes P (bf16) over the S columns it has
-//               read and keeps the row sum in fp32. Part of the exponentials
-//               run as a polynomial on the FMA pipe so that the MUFU and the
-//               issue slots of an SMSP share the work. O is rescaled in TMEM
+//               read and keeps the row sum in fp32. Exponentials use MUFU
+//               ex2 (a polynomial on the FMA pipe for part of them is a build
+//               option, off by default: slower here). O is rescaled in TMEM
 //               only when the running max grows by more than 2^8 (P stays
 //               <= 256, exact in the fp32 accumulator), which after the first
 //               blocks is rare.
