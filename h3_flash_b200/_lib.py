@@ -21,7 +21,7 @@ H3B_OK = 0
 H3B_ERR_VALUE = 1
 H3B_ERR_CUDA = 2
 H3B_ERR_UNSUPPORTED = 3
-ABI_VERSION = 4
+ABI_VERSION = 5
 IPC_HANDLE_BYTES = 64
 
 _p = ctypes.c_void_p
@@ -95,6 +95,10 @@ def load() -> ctypes.CDLL:
         lib.h3b_device_status.restype = ctypes.c_int
         lib.h3b_peer_flags_bytes.argtypes = []
         lib.h3b_peer_flags_bytes.restype = ctypes.c_int64
+        lib.h3b_kernel_launches.argtypes = []
+        lib.h3b_kernel_launches.restype = ctypes.c_int64
+        lib.h3b_reset_kernel_launches.argtypes = []
+        lib.h3b_reset_kernel_launches.restype = None
         version = lib.h3b_abi_version()
         if version != ABI_VERSION:
             raise RuntimeError(f"libh3b.so ABI {version} != expected {ABI_VERSION}")
@@ -104,7 +108,8 @@ def load() -> ctypes.CDLL:
 
 def exported_symbols() -> list[str]:
     return sorted(SIGNATURES) + ["h3b_abi_version", "h3b_last_error", "h3b_device_status",
-                                 "h3b_peer_flags_bytes"]
+                                 "h3b_peer_flags_bytes", "h3b_kernel_launches",
+                                 "h3b_reset_kernel_launches"]
 
 
 def check(code: int, what: str) -> None:
@@ -118,29 +123,21 @@ def check(code: int, what: str) -> None:
     raise RuntimeError(message)
 
 
-_LAUNCHES = 0
-_NON_KERNEL = {"h3b_clear_device_status", "h3b_attention_workspace_size", "h3b_ipc_handle",
-               "h3b_ipc_open", "h3b_ipc_close"}
-
-
 def call(name: str, *args: Any) -> None:
-    """Call an entry point; every successful kernel entry point counts one launch."""
+    """Call an entry point and raise on a failing status."""
 
-    global _LAUNCHES
     check(getattr(load(), name)(*args), name)
-    if name not in _NON_KERNEL:
-        _LAUNCHES += 1
 
 
 def reset_launch_count() -> None:
-    global _LAUNCHES
-    _LAUNCHES = 0
+    load().h3b_reset_kernel_launches()
 
 
 def launch_count() -> int:
-    """h3b kernel launches issued by this process since the last reset."""
+    """h3b kernels launched by this process since the last reset, counted by the
+    library at each launch (an attention call with a split tail launches two)."""
 
-    return _LAUNCHES
+    return int(load().h3b_kernel_launches())
 
 
 def device_status() -> int:

@@ -1,5 +1,6 @@
 // Library-level C ABI plumbing: version, per-thread error string, and the
 // device status word that bounded in-kernel waits report into.
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 #include <string>
@@ -13,12 +14,17 @@ static thread_local std::string t_last_error;
 void set_error(const std::string& msg) { t_last_error = msg; }
 void clear_error() { t_last_error.clear(); }
 
+// Kernels this process has launched through the ABI. Every launcher calls
+// check_launch once after each of its launches, so the count lives here.
+static std::atomic<long long> g_launches{0};
+
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     set_error(std::string(what) + ": " + cudaGetErrorString(e));
     return H3B_ERR_CUDA;
   }
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   return H3B_OK;
 }
 
@@ -46,6 +52,14 @@ unsigned int* status_ptr() {
 }  // namespace h3b
 
 extern "C" int h3b_abi_version(void) { return H3B_ABI_VERSION; }
+
+extern "C" int64_t h3b_kernel_launches(void) {
+  return (int64_t)h3b::g_launches.load(std::memory_order_relaxed);
+}
+
+extern "C" void h3b_reset_kernel_launches(void) {
+  h3b::g_launches.store(0, std::memory_order_relaxed);
+}
 
 extern "C" const char* h3b_last_error(void) { return h3b::t_last_error.c_str(); }
 

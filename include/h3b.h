@@ -30,9 +30,14 @@ typedef struct CUstream_st* h3b_stream_t; /* == cudaStream_t */
 #define H3B_ERR_CUDA 2        /* CUDA launch or driver error: RuntimeError         */
 #define H3B_ERR_UNSUPPORTED 3 /* valid input this build does not handle: RuntimeError */
 
-#define H3B_ABI_VERSION 4
+#define H3B_ABI_VERSION 5
 
 int h3b_abi_version(void);
+/* Kernels launched through this library by this process (all devices and host
+ * threads), counted at launch; h3b_reset_kernel_launches sets it back to 0.
+ * No reference counterpart: instrumentation for benchmarks and tests. */
+int64_t h3b_kernel_launches(void);
+void h3b_reset_kernel_launches(void);
 /* Message of the last failing call on this host thread ("" if none). */
 const char* h3b_last_error(void);
 

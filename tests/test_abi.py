@@ -82,3 +82,13 @@ def test_attention_p2p_argument_errors_without_a_gpu():
         _lib.call("h3b_attention_p2p", ptrs, counts, 17, 0, fake, 1, 128, 0.1, None, 0, None)
     with pytest.raises(RuntimeError, match="head_dim must be 128"):
         _lib.call("h3b_attention_p2p", ptrs, counts, 2, 0, fake, 1, 64, 0.1, None, 0, None)
+
+
+def test_launch_counter_counts_launches_only():
+    """The library counts kernels at launch; calls rejected by validation launch nothing."""
+
+    _lib.reset_launch_count()
+    assert _lib.launch_count() == 0
+    with pytest.raises(ValueError):
+        _lib.call("h3b_pack_qkv", None, None, None, None, 4, 6, 128, 4, 0, 0, 0, 0, 0, 0, None)
+    assert _lib.launch_count() == 0
