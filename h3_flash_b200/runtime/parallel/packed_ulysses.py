@@ -94,6 +94,8 @@ class PackedUlyssesRuntime:
             "output_collectives_per_attention": 1,
             "relayout": "cuda_fused_qknorm_rope_pack" if self.peer is None
             else "cuda_fused_qknorm_rope_pack_p2p",
+            "output_exchange": "nccl_all_to_all_then_merge" if self.peer is None
+            else ("attention_epilogue_p2p" if self.fuse_output_exchange else "scatter_p2p"),
             "attention": "h3b_tcgen05",
             "row_count_collectives_per_request": 1,
             "requests": self.requests,
