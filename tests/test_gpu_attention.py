@@ -122,3 +122,36 @@ def test_split_tail_matches_unsplit_and_oracle():
     _check(whole[0], ref)
     # rows outside the split units come from identical code paths
     assert torch.equal(split[0, :148 * 256], whole[0, :148 * 256])
+
+
+def test_dense_processor_with_the_h3b_kernel_matches_eager_attention():
+    """The dense FA4-profile processor (dense_fa4.py:88-170) with its default kernel,
+    h3b attention, on an H3 attention module: same result as the module's eager forward
+    (torch RMSNorm, RoPE and SDPA) within the bf16 bar."""
+
+    from h3_flash_b200.runtime.attention.dense_fa4 import DenseFA4MiniMaxH3Processor
+    from h3_flash_b200.runtime.h3_block import Attention
+    from h3_flash_b200.workloads import rope_tables
+
+    torch.manual_seed(3)
+    attn = Attention(384, 3, 128).to("cuda", torch.bfloat16).eval()
+    with torch.no_grad():
+        for layer in (attn.to_q, attn.to_k, attn.to_v, attn.to_out[0]):
+            layer.weight.normal_(0.0, 0.05)
+            layer.bias.normal_(0.0, 0.02)
+        attn.norm_q.weight.copy_(1.0 + 0.02 * torch.randn_like(attn.norm_q.weight))
+        attn.norm_k.weight.copy_(1.0 + 0.02 * torch.randn_like(attn.norm_k.weight))
+    rows = 500
+    pos = torch.stack([torch.arange(rows) // 64, (torch.arange(rows) // 8) % 8, torch.arange(rows) % 8], -1)
+    cos, sin = (t.cuda() for t in rope_tables(pos, 96))
+    x = _randn((1, rows, 384), 11)
+    processor = DenseFA4MiniMaxH3Processor()
+    with torch.no_grad():
+        eager = attn(x, (cos, sin))
+        got = processor(attn, x, (cos, sin))
+    assert got.shape == eager.shape and processor.calls == 1
+    diff = (got.float() - eager.float()).abs()
+    half_ulp = eager.float().abs().clamp_min(2.0 ** -126) * 2.0 ** -9
+    assert float((diff - half_ulp).clamp_min(0).max()) <= MAX_ABS
+    cos_sim = torch.nn.functional.cosine_similarity(got.float().flatten(), eager.float().flatten(), dim=0)
+    assert float(cos_sim) >= COSINE
