@@ -366,13 +366,15 @@ def run_h3b(args) -> dict | None:
                          "attention, cuBLAS GEMMs; L2 flushed between steps"}
         torch.cuda.empty_cache()
 
-    install_transformer_fusions(stack, gemm_epilogue=not args.no_gemm_epilogue)
+    gemm_pack = not args.no_gemm_pack
+    install_transformer_fusions(stack, gemm_epilogue=not args.no_gemm_epilogue, gemm_pack=gemm_pack)
     runtime = None
     if world > 1:
         from h3_flash_b200.runtime.parallel import install_packed_ulysses
 
         runtime = install_packed_ulysses(stack, exchange=args.exchange,
-                                         fuse_output_exchange=args.output_exchange == "fused")
+                                         fuse_output_exchange=args.output_exchange == "fused",
+                                         gemm_pack=gemm_pack)
         runtime.begin_request()
 
     def step(x):
@@ -450,19 +452,27 @@ def run_h3b(args) -> dict | None:
                 + 4 * r * d * 2          # residual+rmsnorm+modulate: 2 reads, 2 writes
                 + (2 * r * cfg.ffn_inner * 2 if args.no_gemm_epilogue else 0)  # GELU kernel: read, write
                 + 3 * r * d * 2          # gated residual: 2 reads, 1 write
-                + 2 * 3 * r * d * 2)     # qknorm+rope+pack: read qkv, write packed
-    ew_ms = sum(sum(v) / args.steps for k, v in sections.items() if k in ("elementwise", "qknorm_rope_pack"))
+                + (0 if gemm_pack else 2 * 3 * r * d * 2))  # qknorm+rope+pack: read qkv, write packed
+    ew_keys = ("elementwise",) if gemm_pack else ("elementwise", "qknorm_rope_pack")
+    ew_ms = sum(sum(v) / args.steps for k, v in sections.items() if k in ew_keys)
     ew_ms = _max_over_ranks(ew_ms, world)
-    a2a_bytes = (4 * r * d * 2) * (world - 1) / world if world > 1 else 0.0
-    a2a_ms = _max_over_ranks(sum(sections.get("all_to_all", [0.0])) / max(args.steps, 1), world)
     fused_output = world > 1 and args.exchange == "p2p" and args.output_exchange == "fused"
+    per_row = r * d * 2 * (world - 1) / world if world > 1 else 0.0  # one [r, d] tensor sent
+    a2a_keys = ["all_to_all"]
+    covers = "QKV and output rows"
+    a2a_bytes = 4 * per_row
     if world > 1 and args.exchange == "p2p":
-        # the QKV exchange happens inside the pack kernel: count the whole pack
-        a2a_ms = _max_over_ranks(sum(sections.get("all_to_all", [0.0]) + sections.get("qknorm_rope_pack", [0.0]))
-                                 / max(args.steps, 1), world)
-    if fused_output:
-        # the output rows leave inside the attention kernel, whose time is the attention's
-        a2a_bytes = (3 * r * d * 2) * (world - 1) / world
+        if gemm_pack and fused_output:
+            a2a_bytes, covers = 0.0, ("barriers only: the QKV rows move inside the QKV GEMM kernel, "
+                                      "the output rows inside the attention kernel")
+        elif gemm_pack:
+            a2a_bytes, covers = per_row, "output rows (scatter + barriers); the QKV rows move inside the QKV GEMM"
+        else:
+            a2a_keys.append("qknorm_rope_pack")  # the QKV exchange happens inside the pack kernel
+            if fused_output:
+                a2a_bytes, covers = 3 * per_row, ("QKV rows (pack kernel + barriers); the output rows "
+                                                  "move inside the attention kernel")
+    a2a_ms = _max_over_ranks(sum(sum(sections.get(k, [0.0])) for k in a2a_keys) / max(args.steps, 1), world)
     sections_total = {k: round(sum(v) / args.steps, 4) for k, v in sections.items()}
 
     if rank != 0:
@@ -486,6 +496,8 @@ def run_h3b(args) -> dict | None:
             "dim": cfg.dim, "heads": cfg.heads, "head_dim": cfg.head_dim, "ffn": f"{cfg.ffn_inner} gelu-tanh" + ("" if args.no_gemm_epilogue else " (in the GEMM epilogue)"),
             "rotary_dim": cfg.rotary_dim, "rows_per_rank": rows, "heads_per_rank": hl,
             "parallelism": f"ulysses_sp{world}",
+            "qkv_projection": ("h3b tcgen05 GEMM with QK-norm + RoPE + pack (+ QKV exchange at p2p) in its epilogue"
+                               if gemm_pack else "cuBLAS GEMM, then the h3b QK-norm + RoPE + pack kernel"),
             "exchange": (args.exchange + (" (output exchange in the attention epilogue)" if fused_output else "")
                          if world > 1 else "none"), "l2": "flushed between timed steps (256 MiB write, then read back)",
         },
@@ -521,14 +533,13 @@ def run_h3b(args) -> dict | None:
                                 "frac": round(ew_bytes / (ew_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)
                                 if ew_ms else None},
             "all_to_all_nvlink": {"bytes_sent_per_gpu": a2a_bytes, "ms": round(a2a_ms, 4),
-                                  "achieved_gbs": round(a2a_bytes / (a2a_ms * 1e-3) / 1e9, 1) if a2a_ms else None,
+                                  "achieved_gbs": round(a2a_bytes / (a2a_ms * 1e-3) / 1e9, 1)
+                                  if a2a_ms and a2a_bytes else None,
                                   "peak_gbs": NVLINK_PEER_GBS, "nominal_gbs": 900.0,
                                   "peak_note": "measured peer copy per direction on this pool",
-                                  "covers": ("QKV rows (pack kernel + barriers); the output rows move "
-                                             "inside the attention kernel" if fused_output
-                                             else "QKV and output rows"),
+                                  "covers": covers,
                                   "frac": round(a2a_bytes / (a2a_ms * 1e-3) / 1e9 / NVLINK_PEER_GBS, 4)
-                                  if a2a_ms else None},
+                                  if a2a_ms and a2a_bytes else None},
         },
         "sections_ms_per_step": sections_total,
         "gpu_eager_baseline": eager,
@@ -739,6 +750,8 @@ def main() -> int:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-gemm-epilogue", action="store_true",
                         help="GELU as a separate h3b kernel instead of inside the FFN GEMM")
+    parser.add_argument("--no-gemm-pack", action="store_true",
+                        help="cuBLAS QKV projection + the h3b pack kernel instead of the fused h3b QKV GEMM")
     parser.add_argument("--no-eager-baseline", action="store_true",
                         help="skip timing the unfused torch block at N=1")
     parser.add_argument("--sweep", choices=["elementwise"], help="print the config-2 kernel sweep instead")

@@ -227,3 +227,60 @@ def fused_qknorm_rope_pack(q, k, v, q_weight, k_weight, cos, sin, world, q_eps, 
          ptr(sin32), rows, heads, head_dim, rotary_dim, world, float(q_eps), float(k_eps),
          stream_of(q))
     return out
+
+
+def qkv_gemm_pack_supported(x: torch.Tensor, weight: torch.Tensor, heads: int, head_dim: int,
+                            cos: torch.Tensor | None) -> bool:
+    """Whether ``fused_qkv_gemm_pack`` serves this projection: bf16 CUDA tensors,
+    head_dim 128, an even head count, dim % 64 == 0, rotary_dim 0/64/96/128."""
+
+    rot = 0 if cos is None else cos.shape[-1]
+    return (x.is_cuda and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16
+            and head_dim == 128 and heads % 2 == 0 and x.shape[-1] % 64 == 0
+            and weight.shape == (3 * heads * head_dim, x.shape[-1]) and rot in (0, 64, 96, 128))
+
+
+def qkv_gemm_pack_args(op, x, weight, bias, q_weight, k_weight, cos, sin, heads):
+    """Checks shared by the GEMM packing ops; returns (x2d, weight, bias, rotary_dim, cos32, sin32)."""
+
+    require_cuda(op, x, weight, q_weight, k_weight)
+    require_bf16(op, x, weight, q_weight, k_weight)
+    x2d = x.reshape(-1, x.shape[-1])
+    if x2d.stride(-1) != 1 or x2d.stride(0) % 8 or x2d.data_ptr() % 16:
+        x2d = x2d.contiguous()
+    weight = weight.contiguous()
+    if bias is not None:
+        require_bf16(op, bias)
+        bias = bias.contiguous()
+    if cos is None:
+        return x2d, weight, bias, 0, None, None
+    rotary_dim = cos.shape[-1]
+    cos32 = cos.to(torch.float32).contiguous()
+    sin32 = sin.to(torch.float32).contiguous()
+    if cos32.shape[0] != x2d.shape[0]:
+        raise ValueError(f"{op}: rotary tables have {cos32.shape[0]} rows, x has {x2d.shape[0]}")
+    return x2d, weight, bias, rotary_dim, cos32, sin32
+
+
+def fused_qkv_gemm_pack(x, weight, bias, q_weight, k_weight, cos, sin, heads, world, q_eps, k_eps,
+                        out=None):
+    """The QKV projection with QK-norm + RoPE + the destination-major pack in its
+    epilogue (one tcgen05 GEMM). x [..., dim] (rows flattened), weight [3*heads*128, dim]
+    (to_q | to_k | to_v stacked), bias [3*heads*128] or None. Returns
+    [world, rows, heads/world, 3*128], the layout of ``fused_qknorm_rope_pack``, with the
+    projection kept in fp32 up to the norm (src/h3_flash/runtime/parallel/packed_ulysses.py:166-200)."""
+
+    op = "fused_qkv_gemm_pack"
+    if heads % world:
+        raise ValueError(f"heads ({heads}) must divide Ulysses degree ({world})")
+    x2d, weight, bias, rotary_dim, cos32, sin32 = qkv_gemm_pack_args(op, x, weight, bias, q_weight,
+                                                                    k_weight, cos, sin, heads)
+    rows, dim = x2d.shape
+    if out is None:
+        out = torch.empty((world, rows, heads // world, 3 * 128), dtype=x.dtype, device=x.device)
+    call("h3b_qkv_gemm_pack", ptr(out), world, ptr(x2d), rows, dim, x2d.stride(0), ptr(weight),
+         ptr(bias) if bias is not None else None, ptr(q_weight.contiguous()),
+         ptr(k_weight.contiguous()), ptr(cos32) if cos32 is not None else None,
+         ptr(sin32) if sin32 is not None else None, heads, 128, rotary_dim, float(q_eps),
+         float(k_eps), stream_of(x))
+    return out

@@ -171,7 +171,7 @@ def _patch_blocks(transformer: Any, modulate: bool, swiglu: bool, runtime: dict[
         block.forward = forward
 
 
-def _patch_attention(transformer: Any, runtime: dict[str, Any]) -> None:
+def _patch_attention(transformer: Any, runtime: dict[str, Any], gemm_pack: bool = True) -> None:
     """Single-device attention: fused QK-norm+RoPE (+ pack with W=1) and h3b attention.
     A later ``install_packed_ulysses`` replaces this with the W-rank exchange path."""
 
@@ -181,17 +181,21 @@ def _patch_attention(transformer: Any, runtime: dict[str, Any]) -> None:
         attention = block.attn
 
         def forward(hidden_states, rotary_emb=None, attention_mask=None, *, attention=attention):
-            return ulysses_attention_forward(attention, hidden_states, rotary_emb, attention_mask)
+            return ulysses_attention_forward(attention, hidden_states, rotary_emb, attention_mask,
+                                             gemm_pack=gemm_pack)
 
         attention.forward = forward
 
 
 def install_transformer_fusions(transformer: Any, *, modulate: bool = True, swiglu: bool = True,
-                                qknorm_rope: bool = True, gemm_epilogue: bool = True) -> dict[str, Any]:
+                                qknorm_rope: bool = True, gemm_epilogue: bool = True,
+                                gemm_pack: bool = True) -> dict[str, Any]:
     """kernels/transformer.py:207-228. ``swiglu`` toggles the fused FFN activation
     (SwiGLU for H3, GELU-tanh for the BASELINE block). ``gemm_epilogue`` runs a
     GELU-tanh activation inside the FFN projection GEMM (cuBLASLt epilogue) instead
-    of the h3b elementwise kernel after it; SwiGLU always uses the h3b kernel."""
+    of the h3b elementwise kernel after it; SwiGLU always uses the h3b kernel.
+    ``gemm_pack`` runs the QKV projection, QK-norm + RoPE and the pack as one
+    h3b tcgen05 GEMM where the shapes allow it."""
 
     if not HAVE_CUDA_KERNELS:
         raise RuntimeError("H3 transformer fusions require the h3b CUDA extension (libh3b.so)")
@@ -201,11 +205,12 @@ def install_transformer_fusions(transformer: Any, *, modulate: bool = True, swig
         "swiglu": swiglu,
         "qknorm_rope": qknorm_rope,
         "gemm_epilogue": gemm_epilogue,
+        "gemm_pack": gemm_pack,
         "origin": "B200-native sm_100a kernels (h3b)",
         "gate": {},
     }
     if modulate or swiglu:
         _patch_blocks(transformer, modulate, swiglu, runtime)
     if qknorm_rope:
-        _patch_attention(transformer, runtime)
+        _patch_attention(transformer, runtime, gemm_pack)
     return runtime

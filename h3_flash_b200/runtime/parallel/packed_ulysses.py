@@ -19,6 +19,10 @@ merge are replaced by peer stores over NVLink (peer_exchange.py): the pack
 kernel writes each head row into its owner's receive buffer and the attention
 kernel's epilogue writes each output row into its owner's merged buffer
 (``fuse_output_exchange=False``: a separate scatter kernel after attention).
+
+With ``gemm_pack`` (default) the QKV projection, QK-norm + RoPE and the pack are
+one tcgen05 GEMM (h3b_qkv_gemm_pack): its epilogue writes the send buffer, or
+with p2p every owner's receive buffer, directly.
 """
 
 from __future__ import annotations
@@ -31,7 +35,12 @@ import torch.distributed as dist
 import torch.nn.functional as F
 
 from ..attention.dense import packed_attention
-from ..kernels.fusions import fused_qknorm_rope, fused_qknorm_rope_pack
+from ..kernels.fusions import (
+    fused_qknorm_rope,
+    fused_qknorm_rope_pack,
+    fused_qkv_gemm_pack,
+    qkv_gemm_pack_supported,
+)
 from ..timing import TIMER
 from .context import with_context_parallel_reapplied
 from .relayout import can_pack_qkv, merge_heads, pack_qkv_destination_major
@@ -164,40 +173,49 @@ def _linear_params(layer: Any) -> tuple[torch.Tensor, torch.Tensor | None]:
     return layer.weight, getattr(layer, "bias", None)
 
 
-def qkv_projection(attention: Any, hidden: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
-    """to_q/to_k/to_v as one GEMM against a cached concatenated weight.
-
-    Returns q, k, v views [rows, H, D] into one [rows, 3d] buffer. The cache is
+def qkv_weights(attention: Any) -> tuple[torch.Tensor, torch.Tensor | None] | None:
+    """The stacked [3d, dim] weight and [3d] bias of to_q/to_k/to_v (or of to_qkv),
+    or None when the projections are not plain Linears. The concatenation is cached,
     keyed on the parameters' storage and version counters, so in-place weight
     updates rebuild it."""
 
+    if getattr(attention, "fused_projections", False) and hasattr(attention, "to_qkv"):
+        layer = attention.to_qkv
+        return (layer.weight, getattr(layer, "bias", None)) if isinstance(layer, torch.nn.Linear) else None
+    layers = (attention.to_q, attention.to_k, attention.to_v)
+    if not all(isinstance(layer, torch.nn.Linear) for layer in layers):
+        return None
+    params = [_linear_params(layer) for layer in layers]
+    key = tuple((t.data_ptr(), t._version) if t is not None else None for pair in params for t in pair)
+    cache = attention.__dict__.get("_h3b_qkv_cache")
+    if cache is None or cache[0] != key:
+        with torch.no_grad():
+            weight = torch.cat([w for w, _ in params], dim=0)
+            biases = [b for _, b in params]
+            bias = torch.cat(biases) if all(b is not None for b in biases) else None
+            if bias is None and any(b is not None for b in biases):
+                bias = torch.cat([
+                    b if b is not None else torch.zeros(w.shape[0], dtype=w.dtype, device=w.device)
+                    for w, b in params
+                ])
+        attention.__dict__["_h3b_qkv_cache"] = (key, weight, bias)
+        cache = attention.__dict__["_h3b_qkv_cache"]
+    return cache[1], cache[2]
+
+
+def qkv_projection(attention: Any, hidden: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor]:
+    """to_q/to_k/to_v as one GEMM against the cached stacked weight (``qkv_weights``).
+    Returns q, k, v views [rows, H, D] into one [rows, 3d] buffer."""
+
     heads, head_dim = attention.heads, attention.head_dim
     rows = hidden.shape[0]
+    stacked = qkv_weights(attention)
     if getattr(attention, "fused_projections", False) and hasattr(attention, "to_qkv"):
         qkv = attention.to_qkv(hidden)
+    elif stacked is not None:
+        qkv = F.linear(hidden, stacked[0], stacked[1])
     else:
-        layers = (attention.to_q, attention.to_k, attention.to_v)
-        if all(isinstance(layer, torch.nn.Linear) for layer in layers):
-            params = [_linear_params(layer) for layer in layers]
-            key = tuple(
-                (t.data_ptr(), t._version) if t is not None else None for pair in params for t in pair
-            )
-            cache = attention.__dict__.get("_h3b_qkv_cache")
-            if cache is None or cache[0] != key:
-                with torch.no_grad():
-                    weight = torch.cat([w for w, _ in params], dim=0)
-                    biases = [b for _, b in params]
-                    bias = torch.cat(biases) if all(b is not None for b in biases) else None
-                    if bias is None and any(b is not None for b in biases):
-                        bias = torch.cat([
-                            b if b is not None else torch.zeros(w.shape[0], dtype=w.dtype, device=w.device)
-                            for w, b in params
-                        ])
-                attention.__dict__["_h3b_qkv_cache"] = (key, weight, bias)
-                cache = attention.__dict__["_h3b_qkv_cache"]
-            qkv = F.linear(hidden, cache[1], cache[2])
-        else:
-            qkv = torch.cat([layer(hidden) for layer in layers], dim=-1)
+        qkv = torch.cat([layer(hidden) for layer in (attention.to_q, attention.to_k, attention.to_v)], dim=-1)
     width = heads * head_dim
     q = qkv[:, :width].view(rows, heads, head_dim)
     k = qkv[:, width : 2 * width].view(rows, heads, head_dim)
@@ -215,9 +233,11 @@ def _norm_params(norm: Any) -> tuple[torch.Tensor, float] | None:
 
 def ulysses_attention_forward(attention: Any, hidden_states: torch.Tensor, rotary_emb: Any = None,
                               attention_mask: Any = None, *, runtime: PackedUlyssesRuntime | None = None,
-                              fused_qknorm_rope: bool = True) -> torch.Tensor:
+                              fused_qknorm_rope: bool = True, gemm_pack: bool = True) -> torch.Tensor:
     """The patched ``attn.forward`` body (packed_ulysses.py:150-215). ``runtime=None``
-    runs the same data path on one GPU (no exchange)."""
+    runs the same data path on one GPU (no exchange). ``gemm_pack``: where the shapes
+    allow it, the QKV projection, QK-norm + RoPE and the pack (and, with the p2p
+    exchange, the QKV exchange) run as one GEMM kernel."""
 
     if attention_mask is not None:
         raise RuntimeError("packed Ulysses requires padless dense attention")
@@ -228,30 +248,44 @@ def ulysses_attention_forward(attention: Any, hidden_states: torch.Tensor, rotar
     world = runtime.world if runtime is not None else 1
     if heads % world:
         raise ValueError(f"heads ({heads}) must divide Ulysses degree ({world})")
-    with TIMER.section("gemm"):
-        q, k, v = qkv_projection(attention, hidden_states.reshape(rows_local, -1))
     norm_q, norm_k = _norm_params(attention.norm_q), _norm_params(attention.norm_k)
     cos, sin = rotary_emb if rotary_emb is not None else (None, None)
-    if (world > 1 and runtime.peer is not None and fused_qknorm_rope and norm_q is not None
-            and norm_k is not None and _p2p_supported(head_dim, cos)):
-        output = _peer_attention(runtime, q, k, v, norm_q, norm_k, cos, sin, rows_local, head_dim)
+    x2d = hidden_states.reshape(rows_local, -1)
+    fused_norms = fused_qknorm_rope and norm_q is not None and norm_k is not None
+    stacked = qkv_weights(attention) if (gemm_pack and fused_norms) else None
+    use_gemm = stacked is not None and qkv_gemm_pack_supported(x2d, stacked[0], heads, head_dim, cos)
+    peer = world > 1 and runtime.peer is not None and fused_norms and _p2p_supported(head_dim, cos)
+    if peer:
+        if use_gemm:
+            output = _peer_attention_gemm(runtime, x2d, stacked, norm_q, norm_k, cos, sin, heads, head_dim)
+        else:
+            with TIMER.section("gemm"):
+                q, k, v = qkv_projection(attention, x2d)
+            output = _peer_attention(runtime, q, k, v, norm_q, norm_k, cos, sin, rows_local, head_dim)
         output = output.reshape(batch, rows_local, heads * head_dim).type_as(hidden_states)
         runtime.attention_calls += 1
         with TIMER.section("gemm"):
             return attention.to_out[1](attention.to_out[0](output))
-    with TIMER.section("qknorm_rope_pack"):
-        if fused_qknorm_rope and norm_q is not None and norm_k is not None:
-            send = fused_qknorm_rope_pack(q, k, v, norm_q[0], norm_k[0], cos, sin, world,
-                                          norm_q[1], norm_k[1])
-        else:
-            if rotary_emb is not None and norm_q is not None and norm_k is not None:
-                q = fused_qknorm_rope(q.unsqueeze(0), norm_q[0], cos, sin, norm_q[1]).squeeze(0)
-                k = fused_qknorm_rope(k.unsqueeze(0), norm_k[0], cos, sin, norm_k[1]).squeeze(0)
-            elif rotary_emb is None:
-                q, k = attention.norm_q(q), attention.norm_k(k)
+    if use_gemm:
+        with TIMER.section("qkv_gemm_pack"):
+            send = fused_qkv_gemm_pack(x2d, stacked[0], stacked[1], norm_q[0], norm_k[0], cos, sin,
+                                       heads, world, norm_q[1], norm_k[1])
+    else:
+        with TIMER.section("gemm"):
+            q, k, v = qkv_projection(attention, x2d)
+        with TIMER.section("qknorm_rope_pack"):
+            if fused_norms:
+                send = fused_qknorm_rope_pack(q, k, v, norm_q[0], norm_k[0], cos, sin, world,
+                                              norm_q[1], norm_k[1])
             else:
-                raise RuntimeError("rotary embedding needs RMSNorm-style norm_q/norm_k modules")
-            send = pack_qkv_destination_major(q.contiguous(), k.contiguous(), v.contiguous(), world)
+                if rotary_emb is not None and norm_q is not None and norm_k is not None:
+                    q = fused_qknorm_rope(q.unsqueeze(0), norm_q[0], cos, sin, norm_q[1]).squeeze(0)
+                    k = fused_qknorm_rope(k.unsqueeze(0), norm_k[0], cos, sin, norm_k[1]).squeeze(0)
+                elif rotary_emb is None:
+                    q, k = attention.norm_q(q), attention.norm_k(k)
+                else:
+                    raise RuntimeError("rotary embedding needs RMSNorm-style norm_q/norm_k modules")
+                send = pack_qkv_destination_major(q.contiguous(), k.contiguous(), v.contiguous(), world)
     if world > 1:
         with TIMER.section("all_to_all"):
             packed = packed_qkv_exchange(send, rows_local, runtime)
@@ -274,19 +308,26 @@ def _p2p_supported(head_dim: int, cos: Any) -> bool:
     return head_dim in (64, 128, 256) and rotary_dim % 16 == 0 and (head_dim - rotary_dim) % 16 == 0
 
 
-def _peer_attention(runtime: PackedUlyssesRuntime, q, k, v, norm_q, norm_k, cos, sin,
-                    rows_local: int, head_dim: int) -> torch.Tensor:
-    """pack_p2p -> barrier -> attention_p2p (output exchange in its epilogue) ->
-    barrier, or with ``fuse_output_exchange=False`` attention -> scatter_p2p in
-    place of attention_p2p. Returns [r, H, D]."""
+def _peer_attention_gemm(runtime: PackedUlyssesRuntime, x2d, stacked, norm_q, norm_k, cos, sin,
+                         heads: int, head_dim: int) -> torch.Tensor:
+    """qkv_gemm_pack_p2p (projection + QK-norm + RoPE + QKV exchange) -> barrier ->
+    attention_p2p (or attention -> scatter_p2p) -> barrier. Returns [r, H, D]."""
 
     peer = runtime.peer
-    counts = runtime.row_counts(rows_local)
-    with TIMER.section("qknorm_rope_pack"):
-        peer.pack(q, k, v, norm_q[0], norm_k[0], cos, sin, norm_q[1], norm_k[1], counts)
+    counts = runtime.row_counts(x2d.shape[0])
+    with TIMER.section("qkv_gemm_pack"):
+        peer.pack_gemm(x2d, stacked[0], stacked[1], norm_q[0], norm_k[0], cos, sin, norm_q[1],
+                       norm_k[1], heads, counts)
+    return _peer_exchange_rest(runtime, counts, heads // runtime.world, head_dim)
+
+
+def _peer_exchange_rest(runtime: PackedUlyssesRuntime, counts: list[int], heads_local: int,
+                        head_dim: int) -> torch.Tensor:
+    """Everything after the pack: barrier, attention with the output exchange, barrier."""
+
+    peer = runtime.peer
     with TIMER.section("all_to_all"):
         peer.barrier()
-    heads_local = q.shape[1] // runtime.world
     if runtime.fuse_output_exchange:
         with TIMER.section("attention"):
             merged = peer.attention(counts, heads_local, head_dim)
@@ -301,6 +342,19 @@ def _peer_attention(runtime: PackedUlyssesRuntime, q, k, v, norm_q, norm_k, cos,
     return merged
 
 
+def _peer_attention(runtime: PackedUlyssesRuntime, q, k, v, norm_q, norm_k, cos, sin,
+                    rows_local: int, head_dim: int) -> torch.Tensor:
+    """pack_p2p -> barrier -> attention_p2p (output exchange in its epilogue) ->
+    barrier, or with ``fuse_output_exchange=False`` attention -> scatter_p2p in
+    place of attention_p2p. Returns [r, H, D]."""
+
+    peer = runtime.peer
+    counts = runtime.row_counts(rows_local)
+    with TIMER.section("qknorm_rope_pack"):
+        peer.pack(q, k, v, norm_q[0], norm_k[0], cos, sin, norm_q[1], norm_k[1], counts)
+    return _peer_exchange_rest(runtime, counts, q.shape[1] // runtime.world, head_dim)
+
+
 def _single_node_cuda_group(group: Any) -> bool:
     """True when every rank of ``group`` is a CUDA process on this host (collective)."""
 
@@ -312,14 +366,17 @@ def _single_node_cuda_group(group: Any) -> bool:
 
 
 def install_packed_ulysses(transformer: Any, *, group: Any = None, fused_qknorm_rope: bool = True,
-                           exchange: str = "auto", fuse_output_exchange: bool = True) -> PackedUlyssesRuntime:
+                           exchange: str = "auto", fuse_output_exchange: bool = True,
+                           gemm_pack: bool = True) -> PackedUlyssesRuntime:
     """Replace each block's attention forward with the packed-Ulysses path (packed_ulysses.py:131-220).
 
     ``exchange``: ``"p2p"`` moves rows with peer stores over NVLink (one process
     per GPU on one node, CUDA IPC available), ``"nccl"`` with NCCL all-to-alls;
     ``"auto"`` (collective) picks p2p when all ranks are NCCL ranks on one host.
     ``fuse_output_exchange`` (p2p only): the attention kernel stores its output rows
-    into the owners' merged buffers itself, instead of a scatter kernel after it."""
+    into the owners' merged buffers itself, instead of a scatter kernel after it.
+    ``gemm_pack``: the QKV projection GEMM does QK-norm + RoPE + the pack (and with
+    p2p the QKV exchange) in its epilogue, where the shapes allow it."""
 
     if not (dist.is_available() and dist.is_initialized()):
         raise RuntimeError("packed Ulysses requires an initialized process group")
@@ -337,7 +394,7 @@ def install_packed_ulysses(transformer: Any, *, group: Any = None, fused_qknorm_
             def forward(hidden_states, rotary_emb=None, attention_mask=None, *, attention=attention):
                 return ulysses_attention_forward(
                     attention, hidden_states, rotary_emb, attention_mask,
-                    runtime=runtime, fused_qknorm_rope=fused_qknorm_rope,
+                    runtime=runtime, fused_qknorm_rope=fused_qknorm_rope, gemm_pack=gemm_pack,
                 )
 
             attention.forward = forward

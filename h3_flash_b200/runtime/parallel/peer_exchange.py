@@ -36,7 +36,7 @@ import torch.distributed as dist
 
 from ... import _lib
 from ..._torch import call, ptr, stream_of
-from ..kernels.fusions import qknorm_rope_pack_args
+from ..kernels.fusions import qknorm_rope_pack_args, qkv_gemm_pack_args
 
 _ALIGN = 256
 _FLAG_BYTES = 256
@@ -166,6 +166,31 @@ class PeerExchange:
              total, ptr(q), ptr(k), ptr(v), q.stride(0), k.stride(0), v.stride(0),
              ptr(q_weight.contiguous()), ptr(k_weight.contiguous()), ptr(cos32), ptr(sin32), rows,
              heads, head_dim, rotary_dim, float(q_eps), float(k_eps), stream_of(q))
+
+    def pack_gemm(self, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
+                  q_weight: torch.Tensor, k_weight: torch.Tensor, cos: torch.Tensor | None,
+                  sin: torch.Tensor | None, q_eps: float, k_eps: float, heads: int,
+                  counts: list[int]) -> None:
+        """The QKV projection whose epilogue does QK-norm + RoPE and stores each head
+        row into its owner's receive buffer: projection, pack and QKV exchange in one
+        kernel (the same receive-buffer contents as ``pack`` on the projection,
+        except that the projection is not rounded to bf16 before the norm)."""
+
+        op = "fused_qkv_gemm_pack_p2p"
+        x2d, weight, bias, rotary_dim, cos32, sin32 = qkv_gemm_pack_args(
+            op, x, weight, bias, q_weight, k_weight, cos, sin, heads)
+        rows, dim = x2d.shape
+        if rows != counts[self.rank]:
+            raise ValueError(f"{op}: {rows} local rows, the request says {counts[self.rank]}")
+        if heads % self.world:
+            raise ValueError(f"heads ({heads}) must divide Ulysses degree ({self.world})")
+        total = sum(counts)
+        self.ensure(total, max(counts), heads, 128)
+        call("h3b_qkv_gemm_pack_p2p", self._recv_ptrs, self.world, sum(counts[: self.rank]), total,
+             ptr(x2d), rows, dim, x2d.stride(0), ptr(weight), ptr(bias) if bias is not None else None,
+             ptr(q_weight.contiguous()), ptr(k_weight.contiguous()),
+             ptr(cos32) if cos32 is not None else None, ptr(sin32) if sin32 is not None else None,
+             heads, 128, rotary_dim, float(q_eps), float(k_eps), stream_of(x2d))
 
     def check(self) -> None:
         """Raise if a barrier of an earlier call gave up on a peer (status bit 2,

@@ -30,7 +30,7 @@ typedef struct CUstream_st* h3b_stream_t; /* == cudaStream_t */
 #define H3B_ERR_CUDA 2        /* CUDA launch or driver error: RuntimeError         */
 #define H3B_ERR_UNSUPPORTED 3 /* valid input this build does not handle: RuntimeError */
 
-#define H3B_ABI_VERSION 5
+#define H3B_ABI_VERSION 6
 
 int h3b_abi_version(void);
 /* Kernels launched through this library by this process (all devices and host
@@ -46,7 +46,8 @@ const char* h3b_last_error(void);
  * spinning forever. h3b_device_status() copies it to the host (synchronous);
  * h3b_clear_device_status() zeroes it (stream-ordered). Bits:
  *   1 = attention pipeline wait timed out;
- *   2 = h3b_peer_barrier gave up waiting for a peer (10 s). */
+ *   2 = h3b_peer_barrier gave up waiting for a peer (10 s);
+ *   4 = QKV GEMM pipeline wait timed out. */
 int h3b_device_status(int* status_out);
 int h3b_clear_device_status(h3b_stream_t stream);
 
@@ -130,6 +131,23 @@ int h3b_qknorm_rope_pack(void* send, const void* q, const void* k, const void* v
                          const float* sin, int64_t rows, int64_t heads, int64_t head_dim,
                          int64_t rotary_dim, int64_t world, float q_eps, float k_eps,
                          h3b_stream_t stream);
+
+/* The QKV projection with the pack in its epilogue: one tcgen05 GEMM
+ * y = x w_qkv^T (+ bias), x [rows, dim] (row stride x_row_stride elements),
+ * w_qkv [3*heads*head_dim, dim] (the to_q | to_k | to_v weights stacked, nn.Linear
+ * layout), bias [3*heads*head_dim] or NULL; then QK-norm + RoPE of the q and k
+ * head rows in fp32 and the destination-major store of q, k, v exactly as
+ * h3b_qknorm_rope_pack lays them out (send [world, rows, hl, 3*head_dim]). The
+ * projection is not rounded to bf16 before the norm (one rounding, at the store).
+ * Needs head_dim 128, an even head count, dim % 64 == 0 and rotary_dim in
+ * {0, 64, 96, 128} (else H3B_ERR_UNSUPPORTED).
+ * replaces to_q/to_k/to_v + fused_qknorm_rope (x2) + pack_qkv_destination_major
+ *          packed_ulysses.py:166-200, relayout.py:97-130 */
+int h3b_qkv_gemm_pack(void* send, int64_t world, const void* x, int64_t rows, int64_t dim,
+                      int64_t x_row_stride, const void* w_qkv, const void* bias,
+                      const void* q_weight, const void* k_weight, const float* cos,
+                      const float* sin, int64_t heads, int64_t head_dim, int64_t rotary_dim,
+                      float q_eps, float k_eps, h3b_stream_t stream);
 
 /* out[dst, row, h, :] = (q|k|v)[row, dst*hl + h, :], out is [world, rows, hl, 3*head_dim].
  * q/k/v are [rows, heads, head_dim] with element strides (row, head), last dim contiguous.
@@ -228,6 +246,19 @@ int h3b_qknorm_rope_pack_p2p(void* const* recv_ptrs, int64_t world, int64_t row_
                              const void* q_weight, const void* k_weight, const float* cos,
                              const float* sin, int64_t rows, int64_t heads, int64_t head_dim,
                              int64_t rotary_dim, float q_eps, float k_eps, h3b_stream_t stream);
+
+/* h3b_qkv_gemm_pack with the epilogue storing each head row straight into its
+ * owner's receive buffer, at the layout of h3b_qknorm_rope_pack_p2p: the QKV
+ * exchange runs inside the GEMM, overlapped with the tiles still computing.
+ * Same bits as h3b_qkv_gemm_pack followed by an exchange of its send buffer.
+ * replaces the QKV projection, the pack and the QKV exchange of
+ *          packed_ulysses.py:166-200, :85-108 */
+int h3b_qkv_gemm_pack_p2p(void* const* recv_ptrs, int64_t world, int64_t row_offset,
+                          int64_t total_rows, const void* x, int64_t rows, int64_t dim,
+                          int64_t x_row_stride, const void* w_qkv, const void* bias,
+                          const void* q_weight, const void* k_weight, const float* cos,
+                          const float* sin, int64_t heads, int64_t head_dim,
+                          int64_t rotary_dim, float q_eps, float k_eps, h3b_stream_t stream);
 
 /* out is this rank's attention output [S_total, heads_local, head_dim]
  * (contiguous); global row s, owned by rank o (row_counts[] gives every rank's

@@ -92,3 +92,25 @@ def test_launch_counter_counts_launches_only():
     with pytest.raises(ValueError):
         _lib.call("h3b_pack_qkv", None, None, None, None, 4, 6, 128, 4, 0, 0, 0, 0, 0, 0, None)
     assert _lib.launch_count() == 0
+
+
+def test_qkv_gemm_pack_argument_errors_without_a_gpu():
+    """Shape and layout checks return before any CUDA call."""
+
+    fake = 1 << 20
+    args = dict(x=fake, rows=64, dim=256, stride=256, w=fake, b=None, wq=fake, wk=fake, cos=fake, sin=fake)
+
+    def call(heads, head_dim, rot, world=1, dim=256):
+        _lib.call("h3b_qkv_gemm_pack", fake, world, args["x"], args["rows"], dim, dim, args["w"], None,
+                  args["wq"], args["wk"], args["cos"], args["sin"], heads, head_dim, rot, 1e-6, 1e-6, None)
+
+    with pytest.raises(ValueError, match="must divide Ulysses degree"):
+        call(heads=4, head_dim=128, rot=96, world=3)
+    with pytest.raises(RuntimeError, match="head_dim 128"):
+        call(heads=4, head_dim=64, rot=96)
+    with pytest.raises(RuntimeError, match="even head count"):
+        call(heads=3, head_dim=128, rot=96)
+    with pytest.raises(RuntimeError, match="rotary dimension"):
+        call(heads=4, head_dim=128, rot=48)
+    with pytest.raises(RuntimeError, match="dim % 64"):
+        call(heads=4, head_dim=128, rot=96, dim=200)
