@@ -551,6 +551,7 @@ int prepare(Common& c, const void* x, int64_t rows, int64_t dim, int64_t x_row_s
     return H3B_ERR_UNSUPPORTED;
   }
   H3B_REQUIRE(rows < (1LL << 31) && dim < (1LL << 31), "qkv_gemm_pack: shape exceeds limits");
+  if (rows == 0) return H3B_OK;  // nothing to project; empty tensors may carry null pointers
   H3B_REQUIRE(x != nullptr && w_qkv != nullptr && q_weight != nullptr && k_weight != nullptr,
               "qkv_gemm_pack: null argument");
   H3B_REQUIRE(rotary_dim == 0 || (cos != nullptr && sin != nullptr),
@@ -563,9 +564,7 @@ int prepare(Common& c, const void* x, int64_t rows, int64_t dim, int64_t x_row_s
               "qkv_gemm_pack: x row stride must be >= dim and a multiple of 8");
   const int64_t n = 3 * heads * kHeadDim;
   int rc;
-  if (rows > 0) {
-    if ((rc = make_map(&c.xm, x, dim, rows, x_row_stride, "x")) != H3B_OK) return rc;
-  }
+  if ((rc = make_map(&c.xm, x, dim, rows, x_row_stride, "x")) != H3B_OK) return rc;
   if ((rc = make_map(&c.wm, w_qkv, dim, n, dim, "w")) != H3B_OK) return rc;
   c.p.rows = rows;
   c.p.dim = (int)dim;

@@ -278,6 +278,8 @@ def fused_qkv_gemm_pack(x, weight, bias, q_weight, k_weight, cos, sin, heads, wo
     rows, dim = x2d.shape
     if out is None:
         out = torch.empty((world, rows, heads // world, 3 * 128), dtype=x.dtype, device=x.device)
+    if rows == 0:
+        return out
     call("h3b_qkv_gemm_pack", ptr(out), world, ptr(x2d), rows, dim, x2d.stride(0), ptr(weight),
          ptr(bias) if bias is not None else None, ptr(q_weight.contiguous()),
          ptr(k_weight.contiguous()), ptr(cos32) if cos32 is not None else None,

@@ -114,3 +114,14 @@ def test_qkv_gemm_pack_argument_errors_without_a_gpu():
         call(heads=4, head_dim=128, rot=48)
     with pytest.raises(RuntimeError, match="dim % 64"):
         call(heads=4, head_dim=128, rot=96, dim=200)
+
+
+def test_qkv_gemm_pack_without_rows_is_a_noop_without_a_gpu():
+    """No rows: nothing is projected and no CUDA call is made (empty tensors may carry null pointers)."""
+
+    _lib.reset_launch_count()
+    _lib.call("h3b_qkv_gemm_pack", None, 1, None, 0, 256, 256, None, None, None, None, None, None,
+              2, 128, 96, 1e-6, 1e-6, None)
+    _lib.call("h3b_qkv_gemm_pack_p2p", (ctypes.c_void_p * 1)(1 << 20), 1, 0, 0, None, 0, 256, 256, None, None,
+              None, None, None, None, 2, 128, 96, 1e-6, 1e-6, None)
+    assert _lib.launch_count() == 0
