@@ -7,8 +7,11 @@ rank's receive buffer, merged-output buffer and barrier flags live in one device
 allocation that every other rank maps with CUDA IPC (plain peer mappings).
 Then, per attention call, on the current stream:
 
-  h3b_qknorm_rope_pack_p2p   QK-norm + RoPE, each head row stored straight into
-                             the owning rank's receive buffer [S, hl, 3D]
+  h3b_qkv_gemm_pack_p2p      the QKV projection GEMM; its epilogue does QK-norm +
+                             RoPE and stores each head row straight into the
+                             owning rank's receive buffer [S, hl, 3D] (``pack_gemm``;
+                             ``pack`` is h3b_qknorm_rope_pack_p2p on a projection
+                             made elsewhere)
   h3b_peer_barrier           all peers' rows have landed
   h3b_attention_p2p          attention on the own receive buffer; its epilogue
                              stores each output row into its owner's merged
