@@ -131,3 +131,41 @@ def test_workload_shapes_match_baseline() -> None:
     cos, sin = rope_tables(positions(CONFIGS["cpu-gloo"]), 96)
     assert cos.shape == (4352, 96) and sin.dtype == torch.float32
     assert torch.allclose(cos[:, :48], cos[:, 48:])
+
+
+def test_qkv_weights_stack_cache_and_rebuild() -> None:
+    """The stacked to_q | to_k | to_v weight the QKV GEMM consumes: concatenated once,
+    rebuilt after an in-place update, missing biases filled with zeros."""
+
+    from h3_flash_b200.runtime.parallel.packed_ulysses import qkv_weights
+
+    class Attention(torch.nn.Module):
+        def __init__(self) -> None:
+            super().__init__()
+            self.heads, self.head_dim, self.fused_projections = 2, 4, False
+            self.to_q = torch.nn.Linear(8, 8)
+            self.to_k = torch.nn.Linear(8, 8, bias=False)
+            self.to_v = torch.nn.Linear(8, 8)
+
+    attn = Attention()
+    weight, bias = qkv_weights(attn)
+    assert torch.equal(weight, torch.cat([attn.to_q.weight, attn.to_k.weight, attn.to_v.weight]))
+    assert torch.equal(bias, torch.cat([attn.to_q.bias, torch.zeros(8), attn.to_v.bias]))
+    assert qkv_weights(attn)[0] is weight  # cached
+    with torch.no_grad():
+        attn.to_k.weight.mul_(2.0)
+    rebuilt, _ = qkv_weights(attn)
+    assert rebuilt is not weight and torch.equal(rebuilt[8:16], attn.to_k.weight)
+    attn.to_v = torch.nn.Identity()
+    assert qkv_weights(attn) is None
+
+
+def test_qkv_gemm_pack_supported_shapes() -> None:
+    from h3_flash_b200.runtime.kernels.fusions import qkv_gemm_pack_supported
+
+    x = torch.empty(4, 256, dtype=torch.bfloat16)
+    w = torch.empty(3 * 2 * 128, 256, dtype=torch.bfloat16)
+    cos = torch.empty(4, 96)
+    assert not qkv_gemm_pack_supported(x, w, 2, 128, cos)  # CPU tensors: never
+    if torch.cuda.is_available():  # pragma: no cover - CPU suite
+        assert qkv_gemm_pack_supported(x.cuda(), w.cuda(), 2, 128, cos)
