@@ -135,3 +135,42 @@ def test_qkv_gemm_pack_empty_rows_is_a_noop():
     x, w, b, wq, wk, cos, sin = _inputs(0, 256, 2, 96, True, 1)
     out = fused_qkv_gemm_pack(x, w, b, wq, wk, cos, sin, 2, 1, 1e-6, 1e-6)
     assert out.shape == (1, 0, 2, 384)
+
+
+
+def test_qkv_gemm_pack_matches_the_oracle_reference_path():
+    """Against the oracle of the reference path: the projection rounded to bf16 (what
+    to_q/to_k/to_v return), then oracle.fusions_ref.qknorm_rope (pinned to the reference
+    kernel's golden vectors) and oracle.relayout_ref.pack_qkv. The fused kernel skips the
+    projection's bf16 rounding, so it does not match the oracle to a fixed number of
+    spacings where RoPE cancels. The bars, elementwise against the fp32 evaluation T of
+    the same math:
+    - |fused - T| <= 2^-7 |T| + 1e-3 (one bf16 rounding);
+    - |fused - oracle| <= |oracle - T| + 2^-7 |T| + 1e-3 (the oracle's own error plus one
+      rounding);
+    - on average the fused result is at least as close to T as the oracle path."""
+
+    import numpy as np
+
+    from oracle import fusions_ref, relayout_ref
+    from oracle.bf16 import from_f32, to_f32
+    from h3_flash_b200.runtime.kernels.fusions import fused_qkv_gemm_pack
+
+    rows, dim, heads, world = 300, 512, 4, 2
+    x, w, b, wq, wk, cos, sin = _inputs(rows, dim, heads, 96, True, 21)
+    got = fused_qkv_gemm_pack(x, w, b, wq, wk, cos, sin, heads, world, 1e-6, 1e-6)
+    truth = _reference(x, w, b, wq, wk, cos, sin, heads, world, 1e-6).cpu().numpy()
+    bits = lambda t: t.contiguous().view(torch.int16).cpu().numpy().view(np.uint16)
+    y = to_f32(bits(x)) @ to_f32(bits(w)).T + to_f32(bits(b))
+    proj = from_f32(y.astype(np.float32))  # the bf16 projection the reference normalises
+    hd = heads * 128
+    q, k, v = (proj[:, i * hd:(i + 1) * hd].reshape(rows, heads, 128) for i in range(3))
+    cos_np, sin_np = cos.cpu().numpy(), sin.cpu().numpy()
+    qn = fusions_ref.qknorm_rope(q[None], bits(wq), cos_np, sin_np, 1e-6)[0]
+    kn = fusions_ref.qknorm_rope(k[None], bits(wk), cos_np, sin_np, 1e-6)[0]
+    oracle = to_f32(relayout_ref.pack_qkv(qn, kn, v, world))
+    fused = to_f32(bits(got)).reshape(oracle.shape)
+    one_rounding = np.abs(truth) * 2.0 ** -7 + 1e-3
+    assert int((np.abs(fused - truth) > one_rounding).sum()) == 0
+    assert int((np.abs(fused - oracle) > np.abs(oracle - truth) + one_rounding).sum()) == 0
+    assert float(np.abs(fused - truth).mean()) <= float(np.abs(oracle - truth).mean()) * 1.05
