@@ -54,7 +54,11 @@ constexpr int kBM = 128;        // x rows per CTA (256 per pair)
 constexpr int kBN = 256;        // output columns per tile (two heads)
 constexpr int kBNc = kBN / 2;   // W rows each CTA loads
 constexpr int kBK = 64;         // K per stage: one 128-byte swizzle row
-constexpr int kStages = 6;
+// Shared-memory ring depth (32 KB per stage); a build-time knob for tuning.
+#ifndef H3B_GEMM_STAGES
+#define H3B_GEMM_STAGES 6
+#endif
+constexpr int kStages = H3B_GEMM_STAGES;
 constexpr int kEpiWarps = 4;
 constexpr int kThreads = (2 + kEpiWarps) * 32;
 constexpr int kHeadDim = 128;
