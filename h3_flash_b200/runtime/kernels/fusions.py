@@ -29,10 +29,13 @@ from ..._torch import (
 
 
 def _available() -> bool:
+    """Whether libh3b.so loads (or builds). A missing toolchain, a missing library
+    and an ABI mismatch read as unavailable; the installers then raise."""
+
     try:
         _lib.load()
         return True
-    except Exception:
+    except (OSError, RuntimeError):
         return False
 
 
