@@ -21,6 +21,11 @@ around its launches inside the timed steps. ``cpu_baseline`` times the CPU oracl
 port of the reference path (two gloo ranks) on the BASELINE CPU configuration.
 
 ``--impl reference`` times that CPU port as the reference arm (rank 0 only).
+
+Other modes print their own line: ``--sweep elementwise``,
+``--exchange-bench`` (N>1: the exchange operations alone), ``--transformer-bench``
+(the whole H3 transformer per request: invariant caches at N=1, rank-local I/O at N>1),
+``--profile-kernel`` (one kernel for ncu captures).
 """
 
 from __future__ import annotations
@@ -735,6 +740,102 @@ def exchange_bench(args) -> dict | None:
     }
 
 
+def transformer_bench(args) -> dict | None:
+    """The whole H3 transformer forward per request (text/timestep embedders, ``--layers``
+    blocks, output norm and projections) on the 480p-5s sequence plus 128 text tokens,
+    which times the request-level mechanisms. At N=1: the fused model, then the same model
+    with the invariant caches (f2) on a repeated timestep. At N>1: packed Ulysses + caches
+    with rank-local inputs and the compact output gather (f1), against every rank
+    projecting all inputs and gathering all outputs. CUDA events, max over ranks."""
+
+    import torch.distributed as dist
+
+    from h3_flash_b200.runtime.cache import install_h3_invariant_caches
+    from h3_flash_b200.runtime.h3_model import H3Transformer, make_inputs
+    from h3_flash_b200.runtime.kernels import install_transformer_fusions
+    from h3_flash_b200.workloads import CONFIGS
+
+    rank, world, _ = _dist_setup(args.gpus)
+    cfg = CONFIGS[args.config]
+    text_dim, video_channels, audio_channels, n_text = 4096, 64, 64, 128
+
+    def build():
+        torch.manual_seed(0)
+        model = H3Transformer(cfg.dim, cfg.heads, cfg.head_dim, cfg.ffn_inner, args.layers, text_dim=text_dim,
+                              video_channels=video_channels, audio_channels=audio_channels,
+                              freq_dim=256, freqs_per_axis=16)
+        with torch.no_grad():
+            for name, param in model.named_parameters():
+                if name.endswith(("norm.weight", "norm1.weight", "norm2.weight")) or "norm_q" in name \
+                        or "norm_k" in name:
+                    param.fill_(1.0)
+                elif name.endswith("bias"):
+                    param.zero_()
+                else:
+                    param.normal_(0.0, 0.02)
+        return model.to("cuda", torch.bfloat16).eval()
+
+    probe = build()
+    inputs = make_inputs(probe, n_text=n_text, n_video=cfg.video_tokens, n_audio=cfg.audio_tokens,
+                         text_dim=text_dim, grid=cfg.video_grid, n_timesteps=1, seed=1, device="cuda",
+                         dtype=torch.bfloat16)
+    del probe
+
+    def timed(model, begin) -> float:
+        for _ in range(args.warmup):
+            begin()
+            with torch.no_grad():
+                model(**inputs, return_dict=False)
+        torch.cuda.synchronize()
+        _barrier(world)
+        events = []
+        for _ in range(args.steps):
+            begin()
+            start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            start.record()
+            with torch.no_grad():
+                model(**inputs, return_dict=False)
+            end.record()
+            events.append((start, end))
+        torch.cuda.synchronize()
+        _barrier(world)
+        return _max_over_ranks(statistics.mean(s.elapsed_time(e) for s, e in events), world)
+
+    results = {}
+    if world == 1:
+        model = build()
+        install_transformer_fusions(model)
+        results["fused_ms"] = round(timed(model, lambda: None), 3)
+        caches = install_h3_invariant_caches(model)
+        results["fused_cached_ms"] = round(timed(model, caches.begin_request), 3)
+        results["cache_audit"] = caches.audit()
+    else:
+        from h3_flash_b200.runtime.parallel import install_packed_ulysses, install_rank_local_io
+
+        for name, (local_inputs, compact) in (("rank_local_io_ms", (True, True)), ("full_io_ms", (False, False))):
+            model = build()
+            install_transformer_fusions(model)
+            ulysses = install_packed_ulysses(model, exchange=args.exchange)
+            caches = install_h3_invariant_caches(model)
+            install_rank_local_io(model, group=dist.group.WORLD, rank_local_inputs=local_inputs,
+                                  compact_output_gather=compact)
+
+            def begin(ulysses=ulysses, caches=caches):
+                ulysses.begin_request()
+                caches.begin_request()
+
+            results[name] = round(timed(model, begin), 3)
+            if ulysses.peer is not None:
+                ulysses.peer.close()
+            del model
+            torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    return {"transformer_bench": {"config": cfg.name, "layers": args.layers, "n_gpus": world,
+                                  "tokens": {"text": n_text, "video": cfg.video_tokens, "audio": cfg.audio_tokens},
+                                  "steps": args.steps, "warmup": args.warmup, **results}}
+
+
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__.splitlines()[1])
     parser.add_argument("--gpus", type=int, default=1)
@@ -750,6 +851,9 @@ def main() -> int:
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-gemm-epilogue", action="store_true",
                         help="GELU as a separate h3b kernel instead of inside the FFN GEMM")
+    parser.add_argument("--transformer-bench", action="store_true",
+                        help="time the whole H3 transformer per request (f1/f2 mechanisms) instead")
+    parser.add_argument("--layers", type=int, default=2, help="blocks in --transformer-bench")
     parser.add_argument("--no-gemm-pack", action="store_true",
                         help="cuBLAS QKV projection + the h3b pack kernel instead of the fused h3b QKV GEMM")
     parser.add_argument("--no-eager-baseline", action="store_true",
@@ -777,6 +881,15 @@ def main() -> int:
         return 0
     if args.sweep == "elementwise":
         print(json.dumps(elementwise_sweep(args)), flush=True)
+        return 0
+    if args.transformer_bench:
+        line = transformer_bench(args)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        if args.gpus > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
         return 0
 
     if args.impl == "reference":
