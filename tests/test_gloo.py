@@ -1,7 +1,9 @@
-"""Multi-rank host logic on CPU: world_size-2 gloo process groups.
+"""Multi-rank host logic on CPU: gloo process groups of 2 and 4 ranks.
 
 * the packed-Ulysses row-count protocol and varlen exchange of this package,
   checked bit-for-bit against the reference's own gloo run (tests/golden/ulysses_w2.npz);
+* at 4 ranks with uneven rows (one rank empty): the QKV exchange and the output
+  exchange's all-to-all (+ merge) against the oracle's restatement, bit for bit;
 * the oracle's sharded block equals its single-process block (the CPU/gloo config);
 * failure detection: a peer that dies before a collective surfaces as an error
   within the process-group timeout instead of a hang.
@@ -91,6 +93,49 @@ def test_packed_exchange_matches_reference_gloo_run():
         assert counts == [5, 6]
         assert "row count changed" in changed
         assert per_request == 1
+
+
+ROWS_W4 = [3, 0, 5, 2]  # uneven, one rank without rows
+
+
+def _exchange_round_trip_w4(rank, world):
+    """QKV exchange and the output exchange's all-to-all at W=4 over gloo, with the
+    same seeded inputs on every rank (each rank rebuilds all ranks' inputs)."""
+
+    from h3_flash_b200.runtime.parallel.packed_ulysses import (
+        PackedUlyssesRuntime,
+        _all_to_all_varlen,
+        packed_qkv_exchange,
+    )
+    from oracle import relayout_ref
+
+    heads, d = 8, 16
+    hl = heads // world
+    rng = np.random.default_rng(11)
+    qkv = [[rng.integers(0, 2 ** 16, size=(n, heads, d), dtype=np.uint16) for _ in range(3)] for n in ROWS_W4]
+    sends = [relayout_ref.pack_qkv(q, k, v, world) for q, k, v in qkv]
+    total = sum(ROWS_W4)
+    outputs = [rng.integers(0, 2 ** 16, size=(total, hl, d), dtype=np.uint16) for _ in range(world)]
+    runtime = PackedUlyssesRuntime(dist.group.WORLD)
+    runtime.begin_request()
+    rows = ROWS_W4[rank]
+    recv = packed_qkv_exchange(torch.from_numpy(sends[rank].view(np.int16)).view(torch.bfloat16), rows, runtime)
+    counts = runtime.row_counts(rows)
+    block = hl * d
+    back = _all_to_all_varlen(torch.from_numpy(outputs[rank].view(np.int16)).view(torch.bfloat16),
+                              rows * world * block, [c * block for c in counts], [rows * block] * world,
+                              runtime.group)
+    back = back.view(torch.int16).numpy().view(np.uint16).reshape(world, rows, hl, d)
+    want_recv = relayout_ref.exchange(sends, counts)[rank]
+    want_back = relayout_ref.exchange_back(outputs, counts)[rank]
+    return (bool(np.array_equal(recv.view(torch.int16).numpy().view(np.uint16), want_recv)),
+            bool(np.array_equal(relayout_ref.merge_heads(back), want_back)), counts)
+
+
+def test_exchange_round_trip_at_four_ranks_matches_the_oracle():
+    for recv_ok, back_ok, counts in _run(4, _exchange_round_trip_w4):
+        assert counts == ROWS_W4
+        assert recv_ok and back_ok
 
 
 def _oracle_block(rank, world, params, hidden, idx, cos, sin, cfg):
