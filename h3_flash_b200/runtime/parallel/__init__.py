@@ -3,12 +3,14 @@
 from .context import enable_h3_ulysses, h3_context_parallel_plan
 from .packed_ulysses import PackedUlyssesRuntime, install_packed_ulysses
 from .rank_local_io import RankLocalIORuntime, install_rank_local_io
+from .vae import install_clip_parallel_video_vae
 
 __all__ = [
     "PackedUlyssesRuntime",
     "RankLocalIORuntime",
     "enable_h3_ulysses",
     "h3_context_parallel_plan",
+    "install_clip_parallel_video_vae",
     "install_packed_ulysses",
     "install_rank_local_io",
 ]
