@@ -329,6 +329,80 @@ def _max_over_ranks(value: float, world: int) -> float:
     return float(t.item())
 
 
+def _torch_ulysses_forward(attention, hidden_states, rotary_emb=None, attention_mask=None, *, group, counts):
+    """Packed-Ulysses attention in the reference's structure (packed_ulysses.py:150-215)
+    with torch ops in place of its Triton kernels: torch projections, RMSNorm and RoPE,
+    the permute-copy pack, NCCL all-to-alls, torch SDPA, the permute merge."""
+
+    import torch.distributed as dist
+    import torch.nn.functional as F
+
+    from h3_flash_b200.runtime.h3_block import apply_rotary_emb
+    from h3_flash_b200.runtime.parallel.relayout import pack_qkv_reference
+
+    world = dist.get_world_size(group)
+    rows = hidden_states.shape[1]
+    heads, head_dim = attention.heads, attention.head_dim
+    hl = heads // world
+    x = hidden_states[0]
+    q = attention.norm_q(attention.to_q(x).view(rows, heads, head_dim))
+    k = attention.norm_k(attention.to_k(x).view(rows, heads, head_dim))
+    v = attention.to_v(x).view(rows, heads, head_dim)
+    if rotary_emb is not None:
+        q, k = apply_rotary_emb(q, *rotary_emb), apply_rotary_emb(k, *rotary_emb)
+    send = pack_qkv_reference(q.contiguous(), k.contiguous(), v.contiguous(), world)
+    total = sum(counts)
+    block = hl * 3 * head_dim
+    recv = torch.empty(total * block, dtype=send.dtype, device=send.device)
+    dist.all_to_all_single(recv, send.reshape(-1), [c * block for c in counts], [rows * block] * world,
+                           group=group)
+    packed = recv.view(total, hl, 3 * head_dim)
+    q, k, v = (packed[..., i * head_dim:(i + 1) * head_dim].permute(1, 0, 2).unsqueeze(0) for i in range(3))
+    out = F.scaled_dot_product_attention(q, k, v)[0].permute(1, 0, 2).contiguous()  # [S, hl, D]
+    block = hl * head_dim
+    back = torch.empty(world * rows * block, dtype=out.dtype, device=out.device)
+    dist.all_to_all_single(back, out.reshape(-1), [rows * block] * world, [c * block for c in counts],
+                           group=group)
+    merged = back.view(world, rows, hl, head_dim).permute(1, 0, 2, 3).reshape(1, rows, heads * head_dim)
+    return attention.to_out[1](attention.to_out[0](merged))
+
+
+def eager_sp_baseline(stack, hidden, idx, rotary, rows: int, world: int, flush, steps: int) -> dict:
+    """The unfused block over N ranks with ``_torch_ulysses_forward`` as its attention
+    (collective: every rank calls it). Restores the blocks' attention forwards after."""
+
+    import torch.distributed as dist
+
+    group = dist.group.WORLD
+    counts_t = torch.zeros(world, dtype=torch.long, device="cuda")
+    counts_t[dist.get_rank()] = rows
+    dist.all_reduce(counts_t)
+    counts = [int(c) for c in counts_t.tolist()]
+    saved = []
+    for block in stack.transformer_blocks:
+        attention = block.attn
+        saved.append((attention, attention.__dict__.get("forward")))
+
+        def forward(hidden_states, rotary_emb=None, attention_mask=None, *, attention=attention):
+            return _torch_ulysses_forward(attention, hidden_states, rotary_emb, attention_mask, group=group,
+                                          counts=counts)
+
+        attention.forward = forward
+    try:
+        with torch.no_grad():
+            ms = _timed(lambda: stack(hidden, None, idx, rotary), steps, 3, flush)
+    finally:
+        for attention, original in saved:
+            if original is None:
+                del attention.forward
+            else:
+                attention.forward = original
+    return {"ms_per_step": round(_max_over_ranks(ms, world), 4), "steps": steps, "warmup": 3,
+            "what": "the block unfused over N ranks in the reference's packed-Ulysses structure, torch ops "
+                    "in place of its Triton kernels: torch RMSNorm/RoPE/modulate/GELU, permute-copy pack, "
+                    "NCCL all_to_all_single, torch SDPA, permute merge; L2 flushed between steps"}
+
+
 def run_h3b(args) -> dict | None:
     from h3_flash_b200 import _lib
     from h3_flash_b200.runtime.h3_block import H3BlockStack, H3TransformerBlock
@@ -362,6 +436,9 @@ def run_h3b(args) -> dict | None:
     # torch SDPA and cuBLAS (one GPU only; the reference's own Triton kernels do not
     # run without its source tree).
     eager = None
+    if world > 1 and args.eager_sp_baseline:
+        eager = eager_sp_baseline(stack, hidden, idx, rotary, rows, world, flush, min(args.steps, 5))
+        torch.cuda.empty_cache()
     if world == 1 and not args.no_eager_baseline:
         with torch.no_grad():
             eager_steps = min(args.steps, 5)
@@ -854,6 +931,9 @@ def main() -> int:
     parser.add_argument("--transformer-bench", action="store_true",
                         help="time the whole H3 transformer per request (f1/f2 mechanisms) instead")
     parser.add_argument("--layers", type=int, default=2, help="blocks in --transformer-bench")
+    parser.add_argument("--eager-sp-baseline", action="store_true",
+                        help="N>1: also time the unfused block in the reference's packed-Ulysses structure "
+                             "with torch ops (gpu_eager_baseline)")
     parser.add_argument("--no-gemm-pack", action="store_true",
                         help="cuBLAS QKV projection + the h3b pack kernel instead of the fused h3b QKV GEMM")
     parser.add_argument("--no-eager-baseline", action="store_true",

@@ -27,3 +27,38 @@ def test_reference_arm_prints_the_contract_line():
     base = line["cpu_baseline"]
     assert base["kind"] == "port" and base["cores"] >= 1 and base["sample"]
     assert "workload" in line["config"]
+
+
+def _torch_ulysses_worker(rank, world):
+    import torch
+    import torch.distributed as dist
+
+    sys.path.insert(0, str(ROOT))
+    import bench
+    from h3_flash_b200.runtime.h3_block import Attention
+    from h3_flash_b200.workloads import rope_tables, split_bounds
+
+    torch.manual_seed(0)
+    attention = Attention(64, 4, 16, qk_eps=1e-6).double()
+    rows_total = 23
+    g = torch.Generator().manual_seed(1)
+    x = torch.randn(1, rows_total, 64, generator=g, dtype=torch.float64)
+    pos = torch.stack([torch.arange(rows_total) // 6, (torch.arange(rows_total) // 2) % 3, torch.arange(rows_total) % 2], -1)
+    cos, sin = (t.double() for t in rope_tables(pos, 12))
+    with torch.no_grad():
+        expect = attention(x, (cos, sin))
+        start, stop = split_bounds(rows_total, world, rank)
+        counts = [split_bounds(rows_total, world, r)[1] - split_bounds(rows_total, world, r)[0] for r in range(world)]
+        got = bench._torch_ulysses_forward(attention, x[:, start:stop], (cos[start:stop], sin[start:stop]),
+                                           group=dist.group.WORLD, counts=counts)
+    return float((got - expect[:, start:stop]).abs().max())
+
+
+def test_torch_ulysses_baseline_equals_the_full_sequence_attention():
+    """The opt-in N>1 GPU baseline's attention (reference structure, torch ops, all-to-alls)
+    computes the module's full-sequence attention: two gloo ranks, fp64, uneven rows."""
+
+    from tests.test_gloo import _run
+
+    for diff in _run(2, _torch_ulysses_worker):
+        assert diff <= 1e-12, diff
