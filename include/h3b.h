@@ -224,7 +224,8 @@ int h3b_attention_noalloc(void* out, const void* q, const void* k, const void* v
  * host arrays of `world` device pointers indexed by rank, this rank's own
  * local pointer included; world <= 16. One attention call on every rank runs,
  * on one stream:
- *   h3b_qknorm_rope_pack_p2p -> h3b_peer_barrier -> h3b_attention_p2p on the
+ *   h3b_qkv_gemm_pack_p2p (or a projection of its own, then
+ *   h3b_qknorm_rope_pack_p2p) -> h3b_peer_barrier -> h3b_attention_p2p on the
  *   own receive buffer -> h3b_peer_barrier
  * (or, unfused, h3b_attention then h3b_scatter_heads_p2p in place of
  * h3b_attention_p2p) and then reads its merged buffer. With that order single
