@@ -125,3 +125,24 @@ def test_qkv_gemm_pack_without_rows_is_a_noop_without_a_gpu():
     _lib.call("h3b_qkv_gemm_pack_p2p", (ctypes.c_void_p * 1)(1 << 20), 1, 0, 0, None, 0, 256, 256, None, None,
               None, None, None, None, 2, 128, 96, 1e-6, 1e-6, None)
     assert _lib.launch_count() == 0
+
+
+def test_every_declared_entry_point_has_a_python_signature():
+    """The ctypes layer binds every function the header declares (argument types set)."""
+
+    special = {"h3b_abi_version", "h3b_last_error", "h3b_device_status", "h3b_peer_flags_bytes",
+               "h3b_kernel_launches", "h3b_reset_kernel_launches"}
+    missing = [name for name in declared_functions() if name not in _lib.SIGNATURES and name not in special]
+    assert not missing, missing
+
+
+def test_python_signatures_match_the_header_arity():
+    """Each bound function passes as many arguments as the header declares."""
+
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    arity = {}
+    for name, params in re.findall(r"\b(h3b_[a-z0-9_]+)\s*\(([^)]*)\)\s*;", text):
+        params = params.strip()
+        arity[name] = 0 if params in ("", "void") else len(params.split(","))
+    for name, argtypes in _lib.SIGNATURES.items():
+        assert arity.get(name) == len(argtypes), (name, arity.get(name), len(argtypes))
