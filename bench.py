@@ -726,6 +726,23 @@ def profile_kernel(args) -> None:
     elif args.profile_kernel == "elementwise":
         args.steps, args.warmup = max(args.steps, 1), max(args.warmup, 0)
         elementwise_sweep(args)
+    elif args.profile_kernel == "qkv_gemm":
+        # One rank's QKV projection with the pack epilogue at the SP layout given by
+        # --heads-per-rank (3: the SP8 shape, 6400 rows): x 39 MB, W 57 MB, out 118 MB.
+        from h3_flash_b200.runtime.kernels.fusions import fused_qkv_gemm_pack
+        from h3_flash_b200.workloads import positions, rope_tables
+
+        world = cfg.heads // args.heads_per_rank
+        rows = cfg.seq // world
+        g = torch.Generator(device="cuda").manual_seed(0)
+        x = torch.randn(rows, cfg.dim, device="cuda", generator=g).to(torch.bfloat16)
+        w = (0.02 * torch.randn(3 * cfg.heads * cfg.head_dim, cfg.dim, device="cuda", generator=g)).to(torch.bfloat16)
+        b = (0.02 * torch.randn(3 * cfg.heads * cfg.head_dim, device="cuda", generator=g)).to(torch.bfloat16)
+        norm = torch.ones(cfg.head_dim, device="cuda", dtype=torch.bfloat16)
+        cos, sin = (t[:rows].cuda() for t in rope_tables(positions(cfg), cfg.rotary_dim, cfg.theta))
+        out = torch.empty((world, rows, args.heads_per_rank, 3 * cfg.head_dim), device="cuda", dtype=torch.bfloat16)
+        for _ in range(args.warmup + args.steps):
+            fused_qkv_gemm_pack(x, w, b, norm, norm, cos, sin, cfg.heads, world, cfg.eps, cfg.eps, out=out)
     torch.cuda.synchronize()
     from h3_flash_b200 import _lib
 
@@ -939,7 +956,7 @@ def main() -> int:
     parser.add_argument("--no-eager-baseline", action="store_true",
                         help="skip timing the unfused torch block at N=1")
     parser.add_argument("--sweep", choices=["elementwise"], help="print the config-2 kernel sweep instead")
-    parser.add_argument("--profile-kernel", choices=["attention", "elementwise"],
+    parser.add_argument("--profile-kernel", choices=["attention", "elementwise", "qkv_gemm"],
                         help="launch one kernel family for an ncu capture")
     parser.add_argument("--heads-per-rank", type=int, default=3)
     parser.add_argument("--exchange-bench", action="store_true",
