@@ -122,3 +122,18 @@ def test_install_requires_a_process_group():
 
     with pytest.raises(RuntimeError, match="initialized process group"):
         install_clip_parallel_video_vae(TiledVAE())
+
+
+def test_rank_shares_cover_every_tile_once_in_order():
+    from h3_flash_b200.runtime.parallel.vae import _rank_share
+
+    for n_tiles in range(1, 14):
+        tiles = list(range(n_tiles))
+        for world in range(2, 6):
+            shares = [_rank_share(tiles, world, r) for r in range(world)]
+            per_rank = shares[0][1]
+            assert all(len(s) == per_rank and p == per_rank for s, p in shares)
+            flat = [t for s, _ in shares for t in s]
+            assert flat[:n_tiles] == tiles  # rank order is tile order
+            assert all(t == tiles[-1] for t in flat[n_tiles:])  # padding repeats the last tile
+            assert per_rank * world - n_tiles < world
