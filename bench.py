@@ -140,89 +140,260 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 
 
-def _cpu_worker(rank, world, port, threads, steps, warmup, queue):
-    import torch.distributed as dist
+def cpu_reference_block(config: str, chunks: int, timed: int, warmup: int) -> dict:
+    """The reference path's CPU restatement (the oracle's fp32 block at W=1, every host
+    thread) on the bench's own workload.
+
+    The sequence's query rows are cut into ``chunks`` contiguous chunks; one step runs one
+    chunk through the whole block (``oracle.block_ref.block_forward_rows``: its own AdaLN,
+    projections, QK-norm and RoPE, attention over all S keys, output projection, FFN).
+    Keys and values of every row are projected once before the timed steps (untimed) so a
+    chunk can attend over the full sequence; each timed chunk projects its own rows' keys
+    and values again, so consecutive chunks do exactly the arithmetic of the full block.
+    With ``timed == chunks`` the timed steps cover the sequence once and ``value`` is their
+    summed time: one block forward, measured. With ``timed < chunks`` the first ``timed``
+    chunks are a sample and ``value`` scales their sum by chunks / timed (row-linear)."""
 
     from h3_flash_b200.runtime.h3_block import H3TransformerBlock
-    from h3_flash_b200.workloads import CONFIGS, adaln_indices, init_block_, positions, rope_tables, split_bounds
-    from oracle.block_ref import block_forward, fp32_params
-
-    torch.set_num_threads(threads)
-    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
-                            timeout=datetime.timedelta(seconds=600))
-    cfg = CONFIGS["cpu-gloo"]
-    block = init_block_(H3TransformerBlock(cfg.dim, cfg.heads, cfg.head_dim, cfg.ffn_inner), seed=0)
-    params = fp32_params(block)
-    del block
-    start, stop = split_bounds(cfg.seq, world, rank)
-    g = torch.Generator().manual_seed(1 + start)
-    hidden = torch.randn(stop - start, cfg.dim, generator=g)
-    idx = adaln_indices(cfg)[start:stop]
-    cos, sin = rope_tables(positions(cfg), cfg.rotary_dim, cfg.theta)
-    cos, sin = cos[start:stop], sin[start:stop]
-    kw = dict(heads=cfg.heads, head_dim=cfg.head_dim, eps=cfg.eps, qk_eps=cfg.eps, group=dist.group.WORLD)
-    for _ in range(warmup):
-        block_forward(params, hidden, idx, cos, sin, **kw)
-    results = []
-    for _ in range(steps):
-        timings: dict = {}
-        dist.barrier()
-        t0 = time.perf_counter()
-        block_forward(params, hidden, idx, cos, sin, timings=timings, **kw)
-        dist.barrier()
-        results.append((time.perf_counter() - t0, timings["attention_s"], timings["other_s"]))
-    queue.put((rank, results))
-    dist.destroy_process_group()
-
-
-def cpu_reference_block(steps: int, warmup: int, target_seq: int) -> dict:
-    """Times the oracle block on BASELINE config 1 (S=4,352, W=2 gloo, fp32) and scales each
-    step to ``target_seq`` tokens: attention ~ S^2, everything else ~ S."""
-
-    import socket
-
-    import torch.multiprocessing as mp
-
-    from h3_flash_b200.workloads import CONFIGS
+    from h3_flash_b200.workloads import CONFIGS, adaln_indices, init_block_, positions, rope_tables
+    from oracle.block_ref import block_forward_rows, fp32_params, project_kv
 
     cores = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
-    world = 2
-    threads = max(1, cores // world)
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        port = s.getsockname()[1]
-    ctx = mp.get_context("spawn")
-    queue = ctx.Queue()
-    procs = [ctx.Process(target=_cpu_worker, args=(r, world, port, threads, steps, warmup, queue))
-             for r in range(world)]
-    for p in procs:
-        p.start()
-    per_rank = {}
-    for _ in procs:
-        rank, res = queue.get(timeout=3600)
-        per_rank[rank] = res
-    for p in procs:
-        p.join(timeout=60)
-    seq = CONFIGS["cpu-gloo"].seq
-    ratio = target_seq / seq
-    measured, scaled = [], []
-    for i in range(steps):
-        wall = max(per_rank[r][i][0] for r in per_rank)
-        attn = max(per_rank[r][i][1] for r in per_rank)
-        other = max(wall - attn, 0.0)
-        measured.append(wall * 1e3)
-        scaled.append((attn * ratio * ratio + other * ratio) * 1e3)
-    return {
-        "value": statistics.mean(scaled),
-        "unit": "ms",
-        "cores": threads * world,
-        "kind": "port",
-        "measured_ms_at_sample": statistics.mean(measured),
-        "sample": (f"oracle fp32 block (reference path restated: packed-Ulysses a2a over gloo), BASELINE config 1: "
-                   f"S={seq} (4096 video + 256 audio), W={world} gloo ranks x {threads} threads, d=3072, 24x128, "
-                   f"FFN 12288 GELU-tanh; per-step wall time split into attention (scaled by (S/{seq})^2) and "
-                   f"the rest (scaled by S/{seq}) to S={target_seq}"),
-    }
+    threads_before = torch.get_num_threads()
+    torch.set_num_threads(cores)
+    try:
+        cfg = CONFIGS[config]
+        block = init_block_(H3TransformerBlock(cfg.dim, cfg.heads, cfg.head_dim, cfg.ffn_inner), seed=0)
+        params = fp32_params(block)
+        del block
+        g = torch.Generator().manual_seed(1)
+        hidden = torch.randn(cfg.seq, cfg.dim, generator=g)
+        idx = adaln_indices(cfg)
+        cos, sin = rope_tables(positions(cfg), cfg.rotary_dim, cfg.theta)
+        kw = dict(heads=cfg.heads, head_dim=cfg.head_dim, eps=cfg.eps, qk_eps=cfg.eps)
+        k_all = torch.empty(cfg.seq, cfg.heads, cfg.head_dim)
+        v_all = torch.empty_like(k_all)
+        with torch.no_grad():
+            for a in range(0, cfg.seq, 4096):
+                b = min(a + 4096, cfg.seq)
+                k_all[a:b], v_all[a:b] = project_kv(params, hidden[a:b], idx[a:b], cos[a:b], sin[a:b], **kw)
+        bounds = [(cfg.seq * i // chunks, cfg.seq * (i + 1) // chunks) for i in range(chunks)]
+
+        def run(a, b):
+            block_forward_rows(params, hidden[a:b], idx[a:b], cos[a:b], sin[a:b], k_all, v_all, a, **kw)
+
+        warm_rows = min(bounds[0][1], max(cfg.seq // 4, 1))  # first-touch of the chunk-sized buffers
+        with torch.no_grad():
+            for _ in range(warmup):
+                run(0, warm_rows)
+            step_s = []
+            for a, b in bounds[:timed]:
+                t0 = time.perf_counter()
+                run(a, b)
+                step_s.append(time.perf_counter() - t0)
+    finally:
+        torch.set_num_threads(threads_before)
+    measured_ms = sum(step_s) * 1e3
+    covered = sum(b - a for a, b in bounds[:timed])
+    value = measured_ms * cfg.seq / covered
+    if timed == chunks:
+        sample = (f"the whole {cfg.name} block forward (S={cfg.seq}), measured: {chunks} timed steps each run "
+                  f"{cfg.seq // chunks}-{-(-cfg.seq // chunks)} consecutive query rows through the full block "
+                  f"(their own projections, attention over all S keys, FFN); value = the sum of the steps")
+    else:
+        sample = (f"{covered} of the {cfg.seq} query rows of the {cfg.name} block ({timed} of {chunks} row chunks, "
+                  f"each through the full block with attention over all S keys), measured "
+                  f"{measured_ms:.1f} ms, scaled by rows to the whole block")
+    return {"value": value, "unit": "ms", "cores": cores, "kind": "port", "measured_ms": round(measured_ms, 2),
+            "rows_measured": covered, "scaled": timed != chunks,
+            "chunk_ms": [round(t * 1e3, 2) for t in step_s],
+            "sample": "oracle fp32 restatement of the reference block (W=1, torch CPU ops on every host thread): "
+                      + sample}
+
+
+# ---------------------------------------------------------------------------
+# The reference's own GPU block (its Triton kernels, NCCL all-to-alls, torch SDPA)
+# ---------------------------------------------------------------------------
+
+
+def _reference_site() -> Path | None:
+    """Directory holding the unmodified reference package ``h3_flash``: the offline
+    install under baseline/_ref, or $H3_FLASH_REFERENCE_SITE."""
+
+    for candidate in (os.environ.get("H3_FLASH_REFERENCE_SITE"), ROOT / "baseline" / "_ref"):
+        if candidate and (Path(candidate) / "h3_flash" / "runtime" / "kernels" / "fusions.py").exists():
+            return Path(candidate)
+    return None
+
+
+def _diffusers_stand_in() -> str:
+    """Registers the two Diffusers entry points the reference's installers import, when
+    Diffusers itself is absent. ``dispatch_attention_fn`` keeps Diffusers' native backend
+    semantics ([B, S, H, D] in and out, torch SDPA on the [B, H, S, D] views). The
+    context-parallel hook pair is only called for a model that carries a
+    context-parallel config, which the block stack here does not."""
+
+    try:
+        import diffusers  # noqa: F401
+
+        return "diffusers"
+    except ImportError:
+        pass
+    import types
+
+    import torch.nn.functional as F
+
+    def dispatch_attention_fn(query, key, value, attn_mask=None, dropout_p=0.0, is_causal=False, scale=None,
+                              enable_gqa=False, backend=None, parallel_config=None):
+        if backend is not None or parallel_config is not None:
+            raise RuntimeError("the Diffusers stand-in dispatches the native backend only")
+        out = F.scaled_dot_product_attention(query.permute(0, 2, 1, 3), key.permute(0, 2, 1, 3),
+                                             value.permute(0, 2, 1, 3), attn_mask=attn_mask, dropout_p=dropout_p,
+                                             is_causal=is_causal, scale=scale)
+        return out.permute(0, 2, 1, 3)
+
+    def _no_context_parallel(*args, **kwargs):
+        raise RuntimeError("the Diffusers stand-in has no context-parallel hooks")
+
+    from h3_flash_b200.runtime.h3_block import apply_rotary_emb
+
+    names = ("diffusers", "diffusers.models", "diffusers.models.attention_dispatch",
+             "diffusers.models.transformers", "diffusers.models.transformers.transformer_minimax_h3",
+             "diffusers.hooks", "diffusers.hooks.context_parallel")
+    modules = {name: types.ModuleType(name) for name in names}
+    for name in names:
+        if name != "diffusers" and not name.endswith(("attention_dispatch", "minimax_h3", "context_parallel")):
+            modules[name].__path__ = []  # a package, so its submodules import
+    modules["diffusers"].__path__ = []
+    modules["diffusers.models.attention_dispatch"].dispatch_attention_fn = dispatch_attention_fn
+    # the rotary the reference's first-block numerical gate compares against
+    # (transformer.py:174-190); the rotate-half of the reference's own kernel
+    modules["diffusers.models.transformers.transformer_minimax_h3"]._apply_rotary_emb = apply_rotary_emb
+    modules["diffusers.hooks.context_parallel"].apply_context_parallel = _no_context_parallel
+    modules["diffusers.hooks.context_parallel"].remove_context_parallel = _no_context_parallel
+    for name in names[1:]:
+        parent, _, child = name.rpartition(".")
+        setattr(modules[parent], child, modules[name])
+    sys.modules.update(modules)
+    return "stand-in (native SDPA dispatch; rotate-half rotary for the first-block gate)"
+
+
+def reference_stack(cfg, world: int, device: str = "cuda", dtype: torch.dtype = torch.bfloat16):
+    """The block stack with the reference's own LOSSLESS installers applied: its Triton
+    fusions (transformer.py:207-228; modulate and QK-norm+RoPE on, SwiGLU off for the
+    GELU-tanh FFN, which stays eager) and, for world > 1, its packed Ulysses
+    (packed_ulysses.py:131-220: Triton pack, NCCL all_to_all_single, torch SDPA, Triton
+    merge). Returns (stack, runtime or None, provenance) or raises RuntimeError."""
+
+    site = _reference_site()
+    if site is None:
+        raise RuntimeError("the reference package is not installed under baseline/_ref")
+    if str(site) not in sys.path:
+        sys.path.insert(0, str(site))
+    dispatch = _diffusers_stand_in()
+    import h3_flash
+    from h3_flash.runtime.kernels.transformer import install_transformer_fusions as ref_fusions
+
+    from h3_flash_b200.runtime.h3_block import H3BlockStack, H3TransformerBlock
+    from h3_flash_b200.workloads import init_block_
+
+    block = init_block_(H3TransformerBlock(cfg.dim, cfg.heads, cfg.head_dim, cfg.ffn_inner, eps=cfg.eps,
+                                           qk_eps=cfg.eps), seed=0)
+    stack = H3BlockStack([block.to(device=device, dtype=dtype).eval()])
+    ref_fusions(stack, modulate=True, swiglu=False, qknorm_rope=True)
+    runtime = None
+    if world > 1:
+        import torch.distributed as dist
+        from h3_flash.runtime.parallel.packed_ulysses import install_packed_ulysses as ref_packed
+
+        runtime = ref_packed(stack, group=dist.group.WORLD, fused_qknorm_rope=True)
+        runtime.begin_request()
+    provenance = {"package": str(Path(h3_flash.__file__).resolve().parent.relative_to(ROOT))
+                  if Path(h3_flash.__file__).resolve().is_relative_to(ROOT) else h3_flash.__file__,
+                  "diffusers": dispatch}
+    return stack, runtime, provenance
+
+
+def gpu_reference_block(cfg, hidden, idx, rotary, world: int, flush, steps: int) -> tuple[dict, torch.Tensor | None]:
+    """Times the reference's LOSSLESS block (``reference_stack``) on this rank's rows,
+    every rank taking part. Returns the JSON entry and this rank's output."""
+
+    try:
+        stack, runtime, provenance = reference_stack(cfg, world)
+        with torch.no_grad():
+            ms = _timed(lambda: stack(hidden, None, idx, rotary), steps, 3, flush)
+            out = stack(hidden, None, idx, rotary)
+        torch.cuda.synchronize()
+    except (RuntimeError, ImportError) as error:
+        torch.cuda.empty_cache()
+        return {"unavailable": f"{type(error).__name__}: {str(error).splitlines()[0][:200]}"}, None
+    entry = {"ms_per_step": round(_max_over_ranks(ms, world), 4), "steps": steps, "warmup": 3,
+             "what": "the unmodified reference's LOSSLESS block: its Triton fused_rmsnorm_modulate, "
+                     "fused_qknorm_rope and fused_residual_gate_rmsnorm_modulate"
+                     + (", its packed-Ulysses exchange (Triton pack, NCCL all_to_all_single, Triton merge)"
+                        if world > 1 else "")
+                     + ", torch SDPA, torch Linears, eager GELU-tanh FFN; installed by its own "
+                       "install_transformer_fusions" + (" and install_packed_ulysses" if world > 1 else "")
+                     + " on this package's H3-style block stack; L2 flushed between steps",
+             **provenance}
+    if runtime is not None:
+        entry["reference_provenance"] = runtime.provenance()
+    del stack
+    torch.cuda.empty_cache()
+    return entry, out
+
+
+def attention_ab(cfg, steps: int, flush) -> dict:
+    """Attention alone, this package's kernel against torch SDPA, at the N=1 shape (all
+    heads) and the SP8 per-rank shape (heads / 8) of the joint sequence, in one process
+    under one clock record. SDPA gets the q/k/v views the reference hands it
+    (packed_ulysses.py:201-208: [1, h, S, D] transposed views of the packed buffer);
+    the h3b kernel reads the same packed buffer. FLOP = 4 S^2 h D."""
+
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    from h3_flash_b200.runtime.attention.dense import packed_attention
+
+    out = {}
+    d = cfg.head_dim
+    for label, heads in (("sp1", cfg.heads), ("sp8", cfg.heads // 8)):
+        g = torch.Generator(device="cuda").manual_seed(0)
+        packed = torch.randn(cfg.seq, heads, 3 * d, device="cuda", generator=g).to(torch.bfloat16)
+        q, k, v = (t.transpose(0, 1).unsqueeze(0) for t in packed.split(d, dim=-1))
+        flop = 4.0 * cfg.seq * cfg.seq * heads * d
+        try:
+            choice = SDPBackend(torch._fused_sdp_choice(q, k, v)).name
+        except Exception as error:  # noqa: BLE001 - informational
+            choice = f"unknown ({type(error).__name__})"
+        entry = {"heads": heads, "seq": cfg.seq, "flop": flop, "sdpa_default_backend": choice}
+        arms = {"h3b": lambda: packed_attention(packed, d),
+                "sdpa_default": lambda: F.scaled_dot_product_attention(q, k, v)}
+        for name, backend in (("sdpa_cudnn", SDPBackend.CUDNN_ATTENTION), ("sdpa_flash", SDPBackend.FLASH_ATTENTION)):
+            def call(backend=backend):
+                with sdpa_kernel(backend):
+                    return F.scaled_dot_product_attention(q, k, v)
+            arms[name] = call
+        for name, fn in arms.items():
+            try:
+                ms = _timed(fn, steps, 3, flush)
+            except RuntimeError as error:
+                entry[name] = {"unavailable": str(error).splitlines()[0][:160]}
+                continue
+            entry[name] = {"ms": round(ms, 4), "tflops": round(flop / (ms * 1e-3) / 1e12, 1)}
+        ref = F.scaled_dot_product_attention(q, k, v)[0].transpose(0, 1).float()
+        mine = packed_attention(packed, d).float()
+        delta = (mine - ref).abs()
+        entry["h3b_vs_sdpa"] = {"max_abs": float(delta.max()),
+                                "cosine": float(F.cosine_similarity(mine.flatten(), ref.flatten(), dim=0))}
+        best_sdpa = min((entry[k]["ms"] for k in entry if k.startswith("sdpa_") and isinstance(entry[k], dict)
+                         and "ms" in entry[k]), default=None)
+        if best_sdpa and "ms" in entry.get("h3b", {}):
+            entry["h3b_speedup_vs_best_sdpa"] = round(best_sdpa / entry["h3b"]["ms"], 4)
+        out[label] = entry
+        del packed, q, k, v, ref, mine
+        torch.cuda.empty_cache()
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -432,9 +603,14 @@ def run_h3b(args) -> dict | None:
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device="cuda")
     stream = torch.cuda.current_stream()
 
+    # The reference's own LOSSLESS block on the same rows (every rank takes part).
+    reference, reference_out = (None, None)
+    if not args.no_reference_block:
+        reference, reference_out = gpu_reference_block(cfg, hidden, idx, rotary, world, flush,
+                                                       min(args.steps, 5))
     # The same block before any of this package's kernels are installed: torch ops,
-    # torch SDPA and cuBLAS (one GPU only; the reference's own Triton kernels do not
-    # run without its source tree).
+    # torch SDPA and cuBLAS (N=1), or at N>1 (opt-in) the reference's packed-Ulysses
+    # structure with torch ops in place of its Triton kernels.
     eager = None
     if world > 1 and args.eager_sp_baseline:
         eager = eager_sp_baseline(stack, hidden, idx, rotary, rows, world, flush, min(args.steps, 5))
@@ -511,6 +687,30 @@ def run_h3b(args) -> dict | None:
     e2e_pipelined_ms = pipelined_e2e(step, hidden_host, flush, stream, args.steps, world)
     clocks = sampler.stop() if sampler else None
 
+    if reference_out is not None:
+        import torch.nn.functional as F
+
+        mine = step(hidden).float()
+        delta = (mine - reference_out.float()).abs()
+        stats = torch.tensor([float(delta.max()), float(F.cosine_similarity(
+            mine.flatten(), reference_out.float().flatten(), dim=0))], dtype=torch.float64, device="cuda")
+        if world > 1:
+            import torch.distributed as dist
+
+            stats[1] = -stats[1]
+            dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+            stats[1] = -stats[1]
+        reference["output_vs_h3b"] = {"max_abs": round(float(stats[0]), 6), "cosine": round(float(stats[1]), 7),
+                                      "what": "this rank's block output against the reference block's on the "
+                                              "same inputs and weights (worst rank)"}
+        del mine, delta, reference_out
+    if reference is not None and "ms_per_step" in reference:
+        reference["h3b_speedup"] = round(reference["ms_per_step"] / _max_over_ranks(statistics.mean(step_ms), world), 4)
+    side = {}
+    if world == 1 and not args.no_side_lines:
+        side["attention_ab"] = attention_ab(cfg, min(args.steps, 10), flush)
+        side["block_768p_5s_sp1"] = side_block(stack, "768p-5s", min(args.steps, 3), flush)
+        side["elementwise_sweep"] = elementwise_sweep(argparse.Namespace(steps=min(args.steps, 10), warmup=3))
     status = _lib.device_status()
     if status:
         raise RuntimeError(f"h3b device status {status}: a kernel wait timed out")
@@ -605,6 +805,9 @@ def run_h3b(args) -> dict | None:
             if peaks["source"] == "measured" else "fallback",
             "frac_of_burst": round(achieved / peaks["bf16_tflops"], 4),
             "traffic": traffic,
+            "traffic_source": ("DRAM bytes per launch from the committed ncu capture "
+                               "(profiles/attention_480p5s_sp8.md) scaled by heads; not measured in this run")
+            if traffic is not None else None,
             "flop_per_launch": attn_flop,
             "ms_per_launch": round(attn_ms_max, 4),
         },
@@ -624,11 +827,42 @@ def run_h3b(args) -> dict | None:
                                   if a2a_ms and a2a_bytes else None},
         },
         "sections_ms_per_step": sections_total,
+        "gpu_reference_block": reference,
         "gpu_eager_baseline": eager,
+        **side,
         "gpu_launches": launches,
         "clocks": clocks,
     }
     return result
+
+
+def side_block(stack, config: str, steps: int, flush) -> dict:
+    """The installed (fused) block stack at another BASELINE shape on one GPU: ms per
+    block forward and the in-step attention rate. Inputs seeded like the main line."""
+
+    from h3_flash_b200.runtime.timing import TIMER
+    from h3_flash_b200.workloads import CONFIGS, adaln_indices, positions, rope_tables
+
+    cfg = CONFIGS[config]
+    g = torch.Generator().manual_seed(1)
+    hidden = torch.randn(1, cfg.seq, cfg.dim, generator=g).to(torch.bfloat16).cuda()
+    idx = adaln_indices(cfg).cuda()
+    cos, sin = rope_tables(positions(cfg), cfg.rotary_dim, cfg.theta)
+    rotary = (cos.cuda(), sin.cuda())
+    with torch.no_grad():
+        for _ in range(2):
+            stack(hidden, None, idx, rotary)
+        TIMER.reset()
+        TIMER.enabled = True
+        ms = _timed(lambda: stack(hidden, None, idx, rotary), steps, 0, flush)
+        TIMER.enabled = False
+    attn = statistics.mean(TIMER.milliseconds().get("attention", [float("nan")]))
+    flop = 4.0 * cfg.seq * cfg.seq * cfg.heads * cfg.head_dim
+    del hidden
+    torch.cuda.empty_cache()
+    return {"config": f"{cfg.name}: S={cfg.seq} ({cfg.video_tokens} video + {cfg.audio_tokens} audio), SP1",
+            "ms_per_step": round(ms, 3), "steps": steps, "attention_ms": round(attn, 3),
+            "attention_tflops": round(flop / (attn * 1e-3) / 1e12, 1)}
 
 
 def flush_l2(buf: torch.Tensor) -> None:
@@ -953,6 +1187,10 @@ def main() -> int:
                              "with torch ops (gpu_eager_baseline)")
     parser.add_argument("--no-gemm-pack", action="store_true",
                         help="cuBLAS QKV projection + the h3b pack kernel instead of the fused h3b QKV GEMM")
+    parser.add_argument("--no-reference-block", action="store_true",
+                        help="skip timing the reference's own LOSSLESS GPU block (gpu_reference_block)")
+    parser.add_argument("--no-side-lines", action="store_true",
+                        help="N=1: skip the attention A/B, the 768p-5s block and the elementwise sweep keys")
     parser.add_argument("--no-eager-baseline", action="store_true",
                         help="skip timing the unfused torch block at N=1")
     parser.add_argument("--sweep", choices=["elementwise"], help="print the config-2 kernel sweep instead")
@@ -993,15 +1231,19 @@ def main() -> int:
         rank = int(os.environ.get("RANK", "0"))
         if rank != 0:
             return 0
-        base = cpu_reference_block(max(args.steps, 1), max(args.warmup, 0) and 1, CONFIGS[args.config].seq)
+        steps = max(args.steps, 1)
+        base = cpu_reference_block(args.config, steps, steps, max(args.warmup, 0))
+        value = round(base["value"], 2)
         line = {
-            "metric": METRIC, "impl": "reference", "value": round(base["value"], 2), "unit": "ms",
+            "metric": METRIC, "impl": "reference", "value": value, "unit": "ms",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(base["value"], 2), "higher_is_better": False, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": f"{args.config} DiT block forward (CPU port of the reference path)"},
-            "cpu_baseline": base,
-            "e2e": {"value": round(base["value"], 2), "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+            "ms_per_step": value, "higher_is_better": False, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic: seeded N(0,1) activations, N(0,0.02) weights",
+            "config": {"workload": f"{CONFIGS[args.config].name} DiT block forward (CPU port of the reference path, "
+                                   f"W=1, every host thread)", "seq": CONFIGS[args.config].seq,
+                       "measurement": "the timed steps cover the block's query rows once; value is their sum"},
+            "cpu_baseline": {**base, "value": value},
+            "e2e": {"value": value, "unit": "ms", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
         }
         print(json.dumps(line), flush=True)
         return 0
@@ -1009,7 +1251,7 @@ def main() -> int:
     result = run_h3b(args)
     if result is not None:
         if args.gpus == 1 and not args.no_cpu_baseline:
-            result["cpu_baseline"] = cpu_reference_block(2, 1, CONFIGS[args.config].seq)
+            result["cpu_baseline"] = cpu_reference_block(args.config, 16, 4, 1)
         print(json.dumps(result), flush=True)
     if args.gpus > 1:
         import torch.distributed as dist

@@ -7,7 +7,7 @@ exercised and benchmarked without Diffusers:
 
   block.adaln_proj(temb) -> 6 tables [n_table, d]   (shift/scale/gate msa, shift/scale/gate mlp)
   block.norm1, block.norm2                          RMSNorm(d) (weight, eps)
-  block.attn.{to_q,to_k,to_v,norm_q,norm_k,to_out,heads,head_dim}
+  block.attn.{to_q,to_k,to_v,norm_q,norm_k,to_out,heads,head_dim,processor}
   block.ff.net = [activation-with-.proj, Dropout, Linear]   (GELU-tanh or SwiGLU)
 
 Its own ``forward`` methods are the eager upstream-style math (what a model
@@ -66,6 +66,15 @@ class AdaLNTable(nn.Module):
         return self.table.chunk(6, dim=-1)
 
 
+class AttnProcessor:
+    """Diffusers-style processor handle of an attention module: the attention backend
+    and context-parallel config a dispatcher reads. Neither is set here (native SDPA,
+    no context-parallel hooks)."""
+
+    _attention_backend = None
+    _parallel_config = None
+
+
 class Attention(nn.Module):
     def __init__(self, dim: int, heads: int, head_dim: int, qk_eps: float = 1e-6, bias: bool = True,
                  **factory) -> None:
@@ -73,6 +82,7 @@ class Attention(nn.Module):
         self.heads = heads
         self.head_dim = head_dim
         self.fused_projections = False
+        self.processor = AttnProcessor()
         inner = heads * head_dim
         self.to_q = nn.Linear(dim, inner, bias=bias, **factory)
         self.to_k = nn.Linear(dim, inner, bias=bias, **factory)

@@ -51,8 +51,13 @@ def _rank_share(tiles: list, world: int, rank: int) -> tuple[list, int]:
 
 
 def _latent_tile(z: torch.Tensor, tile: tuple[int, int, int, int], ratio: int) -> torch.Tensor:
+    """The latent window of a tile given in sample pixels: it starts at the floored
+    latent coordinate of the tile's start and spans the floored latent length, so every
+    tile of one length has the same latent size whatever its start (vae.py:75-83)."""
+
     y, h, x, w = tile
-    return z[..., y // ratio:(y + h) // ratio, x // ratio:(x + w) // ratio]
+    y0, x0 = y // ratio, x // ratio
+    return z[..., y0:y0 + h // ratio, x0:x0 + w // ratio]
 
 
 def _error_gate(got: torch.Tensor, expect: torch.Tensor, group: Any) -> dict[str, float]:

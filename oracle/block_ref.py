@@ -126,5 +126,54 @@ def block_forward(p: dict[str, torch.Tensor], hidden: torch.Tensor, idx: torch.T
     return out
 
 
+def project_kv(p: dict[str, torch.Tensor], hidden: torch.Tensor, idx: torch.Tensor, cos: torch.Tensor,
+               sin: torch.Tensor, *, heads: int, head_dim: int, eps: float, qk_eps: float
+               ) -> tuple[torch.Tensor, torch.Tensor]:
+    """Keys (normed and rotated) and values [r, H, D] of ``hidden``'s rows, the
+    k/v half of the attention projections of ``block_forward`` at W=1."""
+
+    rows = hidden.shape[0]
+    shift_msa, scale_msa = p["adaln_proj.table"].chunk(6, dim=-1)[:2]
+    normed = _rms(hidden, p["norm1.weight"], eps) * (1.0 + scale_msa.index_select(0, idx)) \
+        + shift_msa.index_select(0, idx)
+    k = F.linear(normed, p["attn.to_k.weight"], p.get("attn.to_k.bias")).view(rows, heads, head_dim)
+    v = F.linear(normed, p["attn.to_v.weight"], p.get("attn.to_v.bias")).view(rows, heads, head_dim)
+    return _rope(_rms(k, p["attn.norm_k.weight"], qk_eps), cos, sin), v
+
+
+def block_forward_rows(p: dict[str, torch.Tensor], hidden: torch.Tensor, idx: torch.Tensor, cos: torch.Tensor,
+                       sin: torch.Tensor, k_all: torch.Tensor, v_all: torch.Tensor, start: int, *, heads: int,
+                       head_dim: int, eps: float, qk_eps: float, activation: str = "gelu-tanh") -> torch.Tensor:
+    """Rows [start, start + r) of one W=1 ``block_forward`` whose keys and values for
+    every row of the sequence are in ``k_all`` / ``v_all`` [S, H, D].
+
+    The chunk projects its own q, k and v and stores its k and v into ``k_all`` /
+    ``v_all`` at its rows (the same values), then attends over all S keys. A pass over
+    consecutive chunks that cover the sequence therefore does exactly the arithmetic of
+    one full ``block_forward``: every projection once, every (query, key) pair once."""
+
+    rows, d = hidden.shape
+    shift_msa, scale_msa, gate_msa, shift_mlp, scale_mlp, gate_mlp = p["adaln_proj.table"].chunk(6, dim=-1)
+    pick = lambda t: t.index_select(0, idx)  # noqa: E731
+    normed = _rms(hidden, p["norm1.weight"], eps) * (1.0 + pick(scale_msa)) + pick(shift_msa)
+    q = F.linear(normed, p["attn.to_q.weight"], p.get("attn.to_q.bias")).view(rows, heads, head_dim)
+    k = F.linear(normed, p["attn.to_k.weight"], p.get("attn.to_k.bias")).view(rows, heads, head_dim)
+    v = F.linear(normed, p["attn.to_v.weight"], p.get("attn.to_v.bias")).view(rows, heads, head_dim)
+    q = _rope(_rms(q, p["attn.norm_q.weight"], qk_eps), cos, sin)
+    k_all[start:start + rows] = _rope(_rms(k, p["attn.norm_k.weight"], qk_eps), cos, sin)
+    v_all[start:start + rows] = v
+    o = attention_heads(q.contiguous(), k_all, v_all).reshape(rows, heads * head_dim)
+    attn_out = F.linear(o, p["attn.to_out.0.weight"], p.get("attn.to_out.0.bias"))
+    hidden = hidden + pick(gate_msa) * attn_out
+    normed = _rms(hidden, p["norm2.weight"], eps) * (1.0 + pick(scale_mlp)) + pick(shift_mlp)
+    projected = F.linear(normed, p["ff.net.0.proj.weight"], p.get("ff.net.0.proj.bias"))
+    if activation == "gelu-tanh":
+        activated = F.gelu(projected, approximate="tanh")
+    else:
+        value, gate = projected.chunk(2, -1)
+        activated = value * F.silu(gate)
+    return hidden + pick(gate_mlp) * F.linear(activated, p["ff.net.2.weight"], p.get("ff.net.2.bias"))
+
+
 def fp32_params(module: torch.nn.Module) -> dict[str, torch.Tensor]:
     return {name: value.detach().to("cpu", torch.float32) for name, value in module.state_dict().items()}

@@ -12,7 +12,8 @@ ROOT = Path(__file__).resolve().parents[1]
 
 
 def test_reference_arm_prints_the_contract_line():
-    result = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "1", "--warmup", "1"],
+    result = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--config", "cpu-gloo",
+                             "--steps", "2", "--warmup", "1"],
                             cwd=ROOT, capture_output=True, text=True, timeout=600)
     assert result.returncode == 0, result.stderr[-2000:]
     lines = [line for line in result.stdout.splitlines() if line.startswith("{")]
@@ -27,6 +28,9 @@ def test_reference_arm_prints_the_contract_line():
     base = line["cpu_baseline"]
     assert base["kind"] == "port" and base["cores"] >= 1 and base["sample"]
     assert "workload" in line["config"]
+    # the timed steps cover the sequence once: a measurement, not a scaled sample
+    assert base["scaled"] is False and base["rows_measured"] == line["config"]["seq"]
+    assert abs(sum(base["chunk_ms"]) - line["value"]) < 0.05 * line["value"]
 
 
 def _torch_ulysses_worker(rank, world):

@@ -66,9 +66,21 @@ class TiledVAE(nn.Module):
         if not self.use_tiling:
             return self.decoder(self.post_quant_conv(z))
         rows = [[self.decoder(self.post_quant_conv(
-            z[..., y // ratio:(y + h) // ratio, x // ratio:(x + w) // ratio])) for x, w in zip(xs, ws)]
+            z[..., y // ratio:y // ratio + h // ratio, x // ratio:x // ratio + w // ratio])) for x, w in zip(xs, ws)]
             for y, h in zip(ys, hs)]
         return self._stitch_tiles(rows, yo, xo)
+
+
+class OddTiledVAE(TiledVAE):
+    """Tiles of 30 sample pixels with an overlap of 10: neither the tile length nor the
+    tile stride (20) is a multiple of the compression ratio (4), so tile starts fall
+    between latent rows and the latent window must start at the floored coordinate and
+    keep the floored length for every tile to come out the same size."""
+
+    tile_sample_min_height = 30
+    tile_sample_min_width = 30
+    tile_sample_min_overlap_height = 10
+    tile_sample_min_overlap_width = 10
 
 
 def _latent():
@@ -76,10 +88,10 @@ def _latent():
     return torch.randn(1, 4, 2, 22, 30, generator=g, dtype=torch.float64)  # 88 x 120 pixels: 4 x 5 tiles
 
 
-def _decode_worker(rank, world, batched):
+def _decode_worker(rank, world, batched, odd=False):
     from h3_flash_b200.runtime.parallel.vae import install_clip_parallel_video_vae
 
-    vae = TiledVAE()
+    vae = OddTiledVAE() if odd else TiledVAE()
     z = _latent()
     with torch.no_grad():
         expect = vae._decode_clip(z)
@@ -92,9 +104,11 @@ def _decode_worker(rank, world, batched):
 
 @pytest.mark.parametrize("world", [2, 3])
 @pytest.mark.parametrize("batched", [False, True])
-def test_clip_parallel_decode_equals_single_process(world, batched):
-    for equal, max_diff, shape, idempotent, contract, size in _run(world, _decode_worker, batched):
-        assert shape == (1, 3, 2, 88, 120)
+@pytest.mark.parametrize("odd", [False, True])
+def test_clip_parallel_decode_equals_single_process(world, batched, odd):
+    for equal, max_diff, shape, idempotent, contract, size in _run(world, _decode_worker, batched, odd):
+        if not odd:
+            assert shape == (1, 3, 2, 88, 120), shape
         if batched:
             assert max_diff <= 1e-12
         else:
