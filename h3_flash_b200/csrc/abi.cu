@@ -33,20 +33,28 @@ int check_launch(const char* what) {
 // relocatable device code).
 static __device__ unsigned int g_status = 0;
 
-static constexpr int kMaxDevices = 64;
-static unsigned int* g_status_addr[kMaxDevices] = {};
-static std::mutex g_status_mu;
+static ContextSlot g_status_slot[kMaxDevices];
+
+void* current_context() {
+  using GetCurrent = int (*)(void**);  // cuCtxGetCurrent(CUcontext*) -> CUresult
+  static GetCurrent fn = [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      p = nullptr;
+    return reinterpret_cast<GetCurrent>(p);
+  }();
+  void* ctx = nullptr;
+  if (fn == nullptr || fn(&ctx) != 0) return nullptr;
+  return ctx;
+}
 
 unsigned int* status_ptr() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
-  std::lock_guard<std::mutex> lock(g_status_mu);
-  if (g_status_addr[dev] == nullptr) {
+  return static_cast<unsigned int*>(context_cached(g_status_slot, []() -> void* {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_status) != cudaSuccess) return nullptr;
-    g_status_addr[dev] = static_cast<unsigned int*>(p);
-  }
-  return g_status_addr[dev];
+    return cudaGetSymbolAddress(&p, g_status) == cudaSuccess ? p : nullptr;
+  }));
 }
 
 }  // namespace h3b

@@ -986,18 +986,17 @@ int attention_launch(void* out, const void* q, const void* k, const void* v, int
                      "v")) != H3B_OK)
     return rc;
   {
-    static bool attr_set[64] = {};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(
-          attention_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemAlloc);
-      if (e != cudaSuccess) {
-        h3b::set_error(std::string("h3b_attention: cannot reserve shared memory: ") +
-                       cudaGetErrorString(e));
-        return H3B_ERR_CUDA;
-      }
-      if (dev >= 0 && dev < 64) attr_set[dev] = true;
+    // Set once per device and context (a function attribute belongs to the context).
+    static h3b::ContextSlot attr_slots[h3b::kMaxDevices];
+    cudaError_t e = cudaErrorInvalidDevice;
+    if (h3b::context_cached(attr_slots, [&]() -> void* {
+          e = cudaFuncSetAttribute(attention_fwd, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   (int)kSmemAlloc);
+          return e == cudaSuccess ? reinterpret_cast<void*>(1) : nullptr;
+        }) == nullptr) {
+      h3b::set_error(std::string("h3b_attention: cannot reserve shared memory: ") +
+                     cudaGetErrorString(e));
+      return H3B_ERR_CUDA;
     }
   }
   Plan pl = make_plan(batch, seq_q, seq_k, heads);
@@ -1137,32 +1136,27 @@ constexpr int64_t kNoAllocScratchBytes = 20ll << 20;
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 namespace {
-std::mutex g_noalloc_mu;
-void* g_noalloc_addr[64] = {};
+h3b::ContextSlot g_noalloc_slot[h3b::kMaxDevices];
 
 // Device address of g_noalloc_scratch on the current device. The first call on
-// a device looks it up (cudaGetSymbolAddress, with that device current); in
-// host code the array's name is only a host-side stand-in and must never reach
-// a kernel.
+// a device looks it up (cudaGetSymbolAddress, with that device current), and so
+// does the first call after the device's context was re-created (cudaDeviceReset
+// reloads the module, which can move the array); otherwise the cached address is
+// used. In host code the array's name is only a host-side stand-in and must
+// never reach a kernel.
 int noalloc_scratch(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 64) {
-    h3b::set_error("h3b_attention_noalloc: no usable current CUDA device");
+  cudaError_t e = cudaErrorInvalidDevice;
+  void* p = h3b::context_cached(g_noalloc_slot, [&]() -> void* {
+    void* a = nullptr;
+    e = cudaGetSymbolAddress(&a, g_noalloc_scratch);
+    return e == cudaSuccess ? a : nullptr;
+  });
+  if (p == nullptr) {
+    h3b::set_error(std::string("h3b_attention_noalloc: cannot resolve the scratch array: ") +
+                   cudaGetErrorString(e));
     return H3B_ERR_CUDA;
   }
-  std::lock_guard<std::mutex> lock(g_noalloc_mu);
-  if (g_noalloc_addr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess || p == nullptr) {
-      h3b::set_error(std::string("h3b_attention_noalloc: cannot resolve the scratch array: ") +
-                     cudaGetErrorString(e));
-      return H3B_ERR_CUDA;
-    }
-    g_noalloc_addr[dev] = p;
-  }
-  *out = g_noalloc_addr[dev];
+  *out = p;
   return H3B_OK;
 }
 }  // namespace

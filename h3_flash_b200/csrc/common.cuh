@@ -6,6 +6,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 #include "../../include/h3b.h"
@@ -22,6 +23,39 @@ int check_launch(const char* what);
 // Device address of this device's status word (bit flags documented in
 // h3b.h), or nullptr if it cannot be resolved. Defined in abi.cu.
 unsigned int* status_ptr();
+
+// The calling thread's current CUDA context (the driver's handle), or nullptr.
+// Per-device caches of module addresses and function attributes are keyed on
+// it: cudaDeviceReset (or a released and re-created primary context) reloads
+// the module, so a device ordinal alone does not identify a valid entry.
+void* current_context();
+
+// One per-device slot that remembers in which context it was filled. Readers
+// and writers may race (concurrent first calls from several host threads);
+// every field is atomic and filling a slot twice is harmless.
+struct ContextSlot {
+  std::atomic<void*> ctx{nullptr};
+  std::atomic<void*> value{nullptr};
+};
+constexpr int kMaxDevices = 64;
+
+// Runs fill() (which returns the slot's value, or nullptr on failure) when the
+// slot for the current device was not filled in the current context. Returns
+// the value, or nullptr if there is no usable device or fill() failed.
+template <class Fill>
+void* context_cached(ContextSlot (&slots)[kMaxDevices], Fill fill) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  void* ctx = current_context();
+  ContextSlot& slot = slots[dev];
+  if (ctx != nullptr && slot.ctx.load(std::memory_order_acquire) == ctx)
+    return slot.value.load(std::memory_order_acquire);
+  void* v = fill();
+  if (v == nullptr) return nullptr;
+  slot.value.store(v, std::memory_order_release);
+  slot.ctx.store(ctx, std::memory_order_release);
+  return v;
+}
 
 enum : unsigned int { kStatusAttentionTimeout = 1u };
 

@@ -595,19 +595,17 @@ int prepare(Common& c, const void* x, int64_t rows, int64_t dim, int64_t x_row_s
 
 template <int ROT, class Dst>
 int launch_rot(const Common& c, const Dst& d, cudaStream_t stream) {
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(qkv_gemm_kernel<ROT, Dst>,
-                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)kSmemAlloc);
-    if (e != cudaSuccess) {
-      set_error(std::string("h3b_qkv_gemm_pack: cannot reserve shared memory: ") +
-                cudaGetErrorString(e));
-      return H3B_ERR_CUDA;
-    }
-    if (dev >= 0 && dev < 64) attr_set[dev] = true;
+  // Set once per device and context (a function attribute belongs to the context).
+  static ContextSlot attr_slots[kMaxDevices];
+  cudaError_t e = cudaErrorInvalidDevice;
+  if (context_cached(attr_slots, [&]() -> void* {
+        e = cudaFuncSetAttribute(qkv_gemm_kernel<ROT, Dst>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmemAlloc);
+        return e == cudaSuccess ? reinterpret_cast<void*>(1) : nullptr;
+      }) == nullptr) {
+    set_error(std::string("h3b_qkv_gemm_pack: cannot reserve shared memory: ") +
+              cudaGetErrorString(e));
+    return H3B_ERR_CUDA;
   }
   qkv_gemm_kernel<ROT, Dst><<<(unsigned)c.grid, kThreads, kSmemAlloc, stream>>>(c.xm, c.wm,
                                                                                c.p, d);

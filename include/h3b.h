@@ -203,7 +203,9 @@ int h3b_attention_workspace_size(int64_t batch, int64_t seq_q, int64_t seq_k, in
  * file-scope 20 MiB device array that every GPU loading the library keeps
  * until exit; shapes needing more return H3B_ERR_VALUE. The first call on a
  * device resolves the array's device address (cudaGetSymbolAddress): make that
- * first call before any stream capture. All calls on a device share the
+ * first call before any stream capture. The address is cached per device and
+ * context, so the first call after cudaDeviceReset (a new context) resolves it
+ * again; that call too belongs outside a capture. All calls on a device share the
  * array; calls whose kernels overlap on the GPU race, so keep them ordered.
  * Nothing in this path calls cudaMalloc, cudaFree or an allocating library. */
 int h3b_attention_noalloc(void* out, const void* q, const void* k, const void* v,

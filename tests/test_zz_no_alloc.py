@@ -55,6 +55,11 @@ def test_noalloc_matches_allocating_entry_point_twice(seq, hl):
     _lib.call("h3b_attention", ptr(expect), ptr(q), ptr(k), ptr(v), 1, seq, seq, hl, 128,
               *_strides(q, k, v, expect), scale, ptr(ws), need, stream_of(q))
 
+    # The whole-unit plan (no workspace) rounds the tail differently from the split plan.
+    unsplit = torch.empty_like(expect)
+    _lib.call("h3b_attention", ptr(unsplit), ptr(q), ptr(k), ptr(v), 1, seq, seq, hl, 128,
+              *_strides(q, k, v, unsplit), scale, None, 0, stream_of(q))
+
     for _ in range(2):  # the shared array keeps the previous call's contents
         got = torch.full_like(expect, float("nan"))
         _lib.call("h3b_attention_noalloc", ptr(got), ptr(q), ptr(k), ptr(v), 1, seq, seq, hl, 128,
@@ -64,6 +69,10 @@ def test_noalloc_matches_allocating_entry_point_twice(seq, hl):
         assert np.isfinite(m["max_abs"]), m
         assert m["max_abs"] <= MAX_ABS, m
         assert m["cosine"] >= COSINE, m
+        # Same split plan, same kernels: the static array stands in for the caller's
+        # workspace bit for bit, and the split tail really ran through it.
+        assert torch.equal(got, expect)
+        assert not torch.equal(got, unsplit), "the split tail did not run"
     assert _lib.device_status() == 0
 
 
