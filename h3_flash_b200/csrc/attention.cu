@@ -4,13 +4,15 @@
 // One CTA owns two 128-row query tiles of one (batch, head) and streams the
 // whole key/value sequence in 128-row blocks:
 //
-//   warp 8      TMA producer: Q0, Q1 once, then K_j / V_j into separate rings
-//               (K and V stages of 32 KB each, 128B-swizzled).
-//   warp 9      MMA issuer (one thread): S_t = Q_t K_j^T into TMEM, then
-//               O_t += P_t V_j with P_t read from TMEM (A operand) and V_j from
-//               shared memory (MN-major B operand), in two 64-key halves. Tiles
-//               t=0,1 alternate, so the tensor core works on one tile while the
-//               other tile's softmax runs.
+//   warp 8      TMA producer: Q0, Q1 once, then K_j and V_j together into a
+//               two-stage ring (64 KB per stage, 128B-swizzled), one mbarrier
+//               per stage for both: the MMA warp waits once per key block.
+//   warp 9      MMA issuer: the whole warp runs the issue loop (waits, descriptor
+//               arithmetic) and one elected lane issues: S_t = Q_t K_j^T into
+//               TMEM, then O_t += P_t V_j with P_t read from TMEM (A operand) and
+//               V_j from shared memory (MN-major B operand), in two 64-key halves.
+//               Tiles t=0,1 alternate, so the tensor core works on one tile
+//               while the other tile's softmax runs.
 //   warps 0-3   softmax of tile 0, warps 4-7 softmax of tile 1. Warp w owns
 //               TMEM lane quadrant w%4, and each of its threads owns one query
 //               row: it loads the row's 128 scores of a block from TMEM, takes
@@ -61,11 +63,7 @@ constexpr int kBlockM = 128;  // query rows per tile
 constexpr int kBlockN = 128;  // key rows per block
 constexpr int kHeadDim = 128;
 constexpr int kTiles = 2;  // query tiles per CTA
-#ifndef H3B_ATTN_K_STAGES
-#define H3B_ATTN_K_STAGES 2
-#endif
-constexpr int kKStages = H3B_ATTN_K_STAGES;
-constexpr int kVStages = 2;
+constexpr int kStages = 2;  // K/V ring depth (one stage holds K_j and V_j)
 constexpr int kSoftmaxWarps = 4 * kTiles;  // one per TMEM lane quadrant per tile
 constexpr int kThreads = (kSoftmaxWarps + 2) * 32;  // + TMA warp + MMA warp
 constexpr int kLoadWarp = kSoftmaxWarps;
@@ -75,10 +73,10 @@ constexpr uint32_t kTileBytes = kBlockM * kHeadDim * 2;  // 32 KB: two 16 KB swi
 constexpr uint32_t kHalfBytes = kTileBytes / 2;
 constexpr uint32_t kSmemQ = 0;
 constexpr uint32_t kSmemK = kSmemQ + kTiles * kTileBytes;
-constexpr uint32_t kSmemV = kSmemK + kKStages * kTileBytes;
-constexpr uint32_t kSmemBar = kSmemV + kVStages * kTileBytes;
-// barriers: q[2], kfull, kempty, vfull, vempty, s[2], p[2][2], o[2] + tmem slot + abort
-constexpr uint32_t kNumBars = kTiles + 2 * kKStages + 2 * kVStages + 4 * kTiles;
+constexpr uint32_t kSmemV = kSmemK + kStages * kTileBytes;
+constexpr uint32_t kSmemBar = kSmemV + kStages * kTileBytes;
+// barriers: q[2], kvfull[stages], kvempty[stages], s[2], p[2][2], o[2] + tmem slot + abort
+constexpr uint32_t kNumBars = kTiles + 2 * kStages + 4 * kTiles;
 constexpr uint32_t kSmemBytes = kSmemBar + ((kNumBars * 8 + 16 + 127) / 128) * 128;
 constexpr uint32_t kSmemAlloc = kSmemBytes + 1024;  // slack to 1024-align the base
 static_assert(kSmemAlloc <= 232448, "shared memory per CTA");
@@ -227,6 +225,17 @@ __device__ __forceinline__ void mma_commit(uint32_t bar) {
   asm volatile(
       "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
       : "memory");
+}
+
+// One lane of a converged warp (elect.sync over all 32 lanes elects the lowest,
+// lane 0, every time): the lane that issues the warp's MMAs and commits. A
+// commit only tracks MMAs of its own thread, so both must come from that lane.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\telect.sync _|p, 0xffffffff;\n\tselp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
 }
 
 // 32 lanes x 32 consecutive 32-bit TMEM columns -> 32 registers per thread.
@@ -450,18 +459,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t sV = sbase + kSmemV;
   const uint32_t bars = sbase + kSmemBar;
   auto bar_q = [&](int t) { return bars + 8u * t; };
-  auto bar_kfull = [&](int s) { return bars + 8u * (kTiles + s); };
-  auto bar_kempty = [&](int s) { return bars + 8u * (kTiles + kKStages + s); };
-  auto bar_vfull = [&](int s) { return bars + 8u * (kTiles + 2 * kKStages + s); };
-  auto bar_vempty = [&](int s) { return bars + 8u * (kTiles + 2 * kKStages + kVStages + s); };
-  auto bar_s = [&](int t) { return bars + 8u * (kTiles + 2 * kKStages + 2 * kVStages + t); };
+  // bar_kvfull(s): K_j and V_j of stage s landed; bar_kvempty(s): every MMA that
+  // reads stage s (S of both tiles for K, PV of both tiles for V) is done.
+  auto bar_kvfull = [&](int s) { return bars + 8u * (kTiles + s); };
+  auto bar_kvempty = [&](int s) { return bars + 8u * (kTiles + kStages + s); };
+  auto bar_s = [&](int t) { return bars + 8u * (kTiles + 2 * kStages + t); };
   // bar_p(t, h): the softmax of tile t has written P for keys [64h, 64h+64) of the block.
-  auto bar_p = [&](int t, int h) {
-    return bars + 8u * (kTiles + 2 * kKStages + 2 * kVStages + kTiles + 2 * t + h);
-  };
-  auto bar_o = [&](int t) {
-    return bars + 8u * (kTiles + 2 * kKStages + 2 * kVStages + 3 * kTiles + t);
-  };
+  auto bar_p = [&](int t, int h) { return bars + 8u * (kTiles + 2 * kStages + kTiles + 2 * t + h); };
+  auto bar_o = [&](int t) { return bars + 8u * (kTiles + 2 * kStages + 3 * kTiles + t); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + kSmemBar + kNumBars * 8);
   volatile uint32_t* abort_flag = tmem_slot + 1;
 
@@ -490,13 +495,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar_p(t, 1), 4 * 32);
       mbar_init(bar_o(t), 1);
     }
-    for (int s = 0; s < kKStages; ++s) {
-      mbar_init(bar_kfull(s), 1);
-      mbar_init(bar_kempty(s), 1);
-    }
-    for (int s = 0; s < kVStages; ++s) {
-      mbar_init(bar_vfull(s), 1);
-      mbar_init(bar_vempty(s), 1);
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(bar_kvfull(s), 1);
+      mbar_init(bar_kvempty(s), 1);
     }
     *abort_flag = 0u;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -530,99 +531,101 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_4d(dst + kHalfBytes, &q_map, bar_q(t), 64, head, row, batch);
       }
       for (int j = 0; j < n_kv && ok; ++j) {
-        const int ks = j % kKStages, vs = j % kVStages;
-        ok = wait_bar(bar_kempty(ks), ((j / kKStages) & 1) ^ 1, abort_flag, prm.status);
+        const int st = j % kStages;
+        ok = wait_bar(bar_kvempty(st), ((j / kStages) & 1) ^ 1, abort_flag, prm.status);
         if (!ok) break;
-        mbar_expect_tx(bar_kfull(ks), kTileBytes);
-        const uint32_t kdst = sK + ks * kTileBytes;
+        mbar_expect_tx(bar_kvfull(st), 2 * kTileBytes);
+        const uint32_t kdst = sK + st * kTileBytes;
+        const uint32_t vdst = sV + st * kTileBytes;
         const int key0 = (j0 + j) * kBlockN;
-        tma_load_4d(kdst, &k_map, bar_kfull(ks), 0, head, key0, batch);
-        tma_load_4d(kdst + kHalfBytes, &k_map, bar_kfull(ks), 64, head, key0, batch);
-        ok = wait_bar(bar_vempty(vs), ((j / kVStages) & 1) ^ 1, abort_flag, prm.status);
-        if (!ok) break;
-        mbar_expect_tx(bar_vfull(vs), kTileBytes);
-        const uint32_t vdst = sV + vs * kTileBytes;
-        tma_load_4d(vdst, &v_map, bar_vfull(vs), 0, head, key0, batch);
-        tma_load_4d(vdst + kHalfBytes, &v_map, bar_vfull(vs), 64, head, key0, batch);
+        tma_load_4d(kdst, &k_map, bar_kvfull(st), 0, head, key0, batch);
+        tma_load_4d(kdst + kHalfBytes, &k_map, bar_kvfull(st), 64, head, key0, batch);
+        tma_load_4d(vdst, &v_map, bar_kvfull(st), 0, head, key0, batch);
+        tma_load_4d(vdst + kHalfBytes, &v_map, bar_kvfull(st), 64, head, key0, batch);
       }
     }
   } else if (warp == kMmaWarp) {
-    if (lane == 0) {
-      // ---------------- MMA issuer ----------------
-      constexpr uint32_t idesc_qk = instr_desc(false);
-      constexpr uint32_t idesc_pv = instr_desc(true);
-      bool ok = true;
-      for (int t = 0; t < kTiles && ok; ++t) ok = wait_bar(bar_q(t), 0, abort_flag, prm.status);
-      // Descriptors are built once: the issue loop only adds compile-time K-step
-      // offsets (a single thread must issue one MMA per 64 clocks to keep the
-      // tensor pipe full, so no descriptor arithmetic on the critical path).
-      // K-major SW128 tiles: K step kk sits at (kk/4) * 16 KB + (kk%4) * 32 B.
-      // MN-major V tile: K step kk (16 keys) sits at kk * 2 KB; N halves 16 KB apart.
-      // (The address field is the low 14 bits of (addr >> 4); every operand lies
-      // below 256 KB, so adding an address delta >> 4 never carries out of it.)
-      const uint64_t q_desc0 = smem_desc(sQ, 16, 1024);
-      const uint64_t k_desc0 = smem_desc(sK, 16, 1024);
-      const uint64_t v_desc0 = smem_desc(sV, kHalfBytes, 1024);
-      // S_t = Q_t K_j^T : 8 MMAs of K=16 over the 128 head dims.
-      auto issue_s = [&](int t, int j) {
-        const uint64_t qd = q_desc0 + (uint64_t)((t * kTileBytes) >> 4);
-        const uint64_t kd = k_desc0 + (uint64_t)(((j % kKStages) * kTileBytes) >> 4);
-        const uint32_t d = tmem + kTmemS + t * 128;
+    // ---------------- MMA issuer ----------------
+    // The whole warp runs the loop (every wait, all descriptor arithmetic, so the
+    // operands are warp-uniform) and one elected lane issues each group of MMAs.
+    // A single issuing thread must keep a shallow tensor-core queue fed, so the
+    // loop waits on as few barriers per key block as it can: one for K_j and V_j
+    // together, two for the P halves of each tile.
+    constexpr uint32_t idesc_qk = instr_desc(false);
+    constexpr uint32_t idesc_pv = instr_desc(true);
+    auto wait_all = [&](uint32_t bar, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, wait_bar(bar, parity, abort_flag, prm.status));
+    };
+    bool ok = true;
+    for (int t = 0; t < kTiles && ok; ++t) ok = wait_all(bar_q(t), 0);
+    // Descriptors are built once: the loop only adds compile-time K-step offsets.
+    // K-major SW128 tiles: K step kk sits at (kk/4) * 16 KB + (kk%4) * 32 B.
+    // MN-major V tile: K step kk (16 keys) sits at kk * 2 KB; N halves 16 KB apart.
+    // (The address field is the low 14 bits of (addr >> 4); every operand lies
+    // below 256 KB, so adding an address delta >> 4 never carries out of it.)
+    const uint64_t q_desc0 = smem_desc(sQ, 16, 1024);
+    const uint64_t k_desc0 = smem_desc(sK, 16, 1024);
+    const uint64_t v_desc0 = smem_desc(sV, kHalfBytes, 1024);
+    // S_t = Q_t K_j^T : 8 MMAs of K=16 over the 128 head dims, then its commit.
+    auto issue_s = [&](int t, int j) {
+      const uint64_t qd = q_desc0 + (uint64_t)((t * kTileBytes) >> 4);
+      const uint64_t kd = k_desc0 + (uint64_t)(((j % kStages) * kTileBytes) >> 4);
+      const uint32_t d = tmem + kTmemS + t * 128;
+      if (elect_one()) {
 #pragma unroll
         for (int kk = 0; kk < kHeadDim / 16; ++kk) {
           const uint64_t off = (uint64_t)(((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4);
           mma_ss(d, qd + off, kd + off, idesc_qk, kk > 0 ? 1u : 0u);
         }
-      };
-      // O_t += P_t V_j over keys [64h, 64h+64): 4 MMAs of K=16; P of keys
-      // [16kk, 16kk+16) is S_t columns [8kk, 8kk+8).
-      auto issue_pv = [&](int t, int j, int h) {
-        const uint64_t vd = v_desc0 + (uint64_t)(((j % kVStages) * kTileBytes) >> 4);
-        const uint32_t d = tmem + kTmemO + t * 128;
+        mma_commit(bar_s(t));
+      }
+      __syncwarp();
+    };
+    // O_t += P_t V_j over keys [64h, 64h+64): 4 MMAs of K=16; P of keys
+    // [16kk, 16kk+16) is S_t columns [8kk, 8kk+8).
+    auto issue_pv = [&](int t, int j, int h) {
+      const uint64_t vd = v_desc0 + (uint64_t)(((j % kStages) * kTileBytes) >> 4);
+      const uint32_t d = tmem + kTmemO + t * 128;
+      if (elect_one()) {
 #pragma unroll
         for (int k4 = 0; k4 < kBlockN / 32; ++k4) {
           const int kk = h * (kBlockN / 32) + k4;
-          mma_ts(d, tmem + kTmemS + t * 128 + kk * 8, vd + (uint64_t)((kk * 2048) >> 4),
-                 idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(d, tmem + kTmemS + t * 128 + kk * 8, vd + (uint64_t)((kk * 2048) >> 4), idesc_pv,
+                 (j > 0 || kk > 0) ? 1u : 0u);
         }
-      };
-      if (ok) ok = wait_bar(bar_kfull(0), 0, abort_flag, prm.status);
-      if (ok) {
-        tc_fence_after();
-        for (int t = 0; t < kTiles; ++t) {
-          issue_s(t, 0);
-          mma_commit(bar_s(t));
-        }
-        mma_commit(bar_kempty(0));
       }
-      for (int j = 0; j < n_kv && ok; ++j) {
-        for (int t = 0; t < kTiles && ok; ++t) {
-          ok = wait_bar(bar_p(t, 0), j & 1, abort_flag, prm.status);
-          if (!ok) break;
+      __syncwarp();
+    };
+    auto commit = [&](uint32_t bar) {
+      if (elect_one()) mma_commit(bar);
+      __syncwarp();
+    };
+    if (ok) ok = wait_all(bar_kvfull(0), 0);
+    if (ok) {
+      tc_fence_after();
+      for (int t = 0; t < kTiles; ++t) issue_s(t, 0);
+    }
+    for (int j = 0; j < n_kv && ok; ++j) {
+      for (int t = 0; t < kTiles && ok; ++t) {
+        ok = wait_all(bar_p(t, 0), j & 1);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(t, j, 0);
+        ok = wait_all(bar_p(t, 1), j & 1);
+        if (!ok) break;
+        tc_fence_after();
+        issue_pv(t, j, 1);
+        // Stage j % kStages is free once both tiles' PV (and, earlier, S) read it.
+        if (t == kTiles - 1) commit(bar_kvempty(j % kStages));
+        if (j + 1 < n_kv) {
           if (t == 0) {
-            ok = wait_bar(bar_vfull(j % kVStages), (j / kVStages) & 1, abort_flag, prm.status);
+            ok = wait_all(bar_kvfull((j + 1) % kStages), ((j + 1) / kStages) & 1);
             if (!ok) break;
+            tc_fence_after();
           }
-          tc_fence_after();
-          issue_pv(t, j, 0);
-          ok = wait_bar(bar_p(t, 1), j & 1, abort_flag, prm.status);
-          if (!ok) break;
-          tc_fence_after();
-          issue_pv(t, j, 1);
-          if (t == kTiles - 1) mma_commit(bar_vempty(j % kVStages));
-          if (j + 1 < n_kv) {
-            if (t == 0) {
-              ok = wait_bar(bar_kfull((j + 1) % kKStages), ((j + 1) / kKStages) & 1,
-                            abort_flag, prm.status);
-              if (!ok) break;
-              tc_fence_after();
-            }
-            issue_s(t, j + 1);
-            mma_commit(bar_s(t));
-            if (t == kTiles - 1) mma_commit(bar_kempty((j + 1) % kKStages));
-          } else {
-            mma_commit(bar_o(t));
-          }
+          issue_s(t, j + 1);
+        } else {
+          commit(bar_o(t));
         }
       }
     }
