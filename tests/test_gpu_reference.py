@@ -201,8 +201,8 @@ def test_block_against_reference_lossless_block(ref):
     assert "baseline" in provenance["package"] or "h3_flash" in provenance["package"]
     block = init_block_(H3TransformerBlock(cfg.dim, cfg.heads, cfg.head_dim, cfg.ffn_inner, eps=cfg.eps,
                                            qk_eps=cfg.eps), seed=0)
-    params = fp32_params(block)
     stack = H3BlockStack([block.to("cuda", torch.bfloat16).eval()])
+    params = fp32_params(block)  # the bf16 weights the GPU blocks use, in fp32
     install_transformer_fusions(stack)
     g = torch.Generator().manual_seed(1)
     hidden = torch.randn(1, cfg.seq, cfg.dim, generator=g).to(torch.bfloat16)
