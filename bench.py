@@ -709,6 +709,7 @@ def run_h3b(args) -> dict | None:
     side = {}
     if world == 1 and not args.no_side_lines:
         side["attention_ab"] = attention_ab(cfg, min(args.steps, 10), flush)
+        side["gemm_ab"] = gemm_ab(cfg, min(args.steps, 10), flush)
         side["block_768p_5s_sp1"] = side_block(stack, "768p-5s", min(args.steps, 3), flush)
         side["elementwise_sweep"] = elementwise_sweep(argparse.Namespace(steps=min(args.steps, 10), warmup=3))
     status = _lib.device_status()
@@ -733,7 +734,7 @@ def run_h3b(args) -> dict | None:
     ew_bytes = (2 * r * d * 2            # rmsnorm_modulate: read x, write
                 + 4 * r * d * 2          # residual+rmsnorm+modulate: 2 reads, 2 writes
                 + (2 * r * cfg.ffn_inner * 2 if args.no_gemm_epilogue else 0)  # GELU kernel: read, write
-                + 3 * r * d * 2          # gated residual: 2 reads, 1 write
+                + (3 * r * d * 2 if args.no_gemm_epilogue else 0)  # gated residual (else in the FFN GEMM)
                 + (0 if gemm_pack else 2 * 3 * r * d * 2))  # qknorm+rope+pack: read qkv, write packed
     ew_keys = ("elementwise",) if gemm_pack else ("elementwise", "qknorm_rope_pack")
     ew_ms = sum(sum(v) / args.steps for k, v in sections.items() if k in ew_keys)
@@ -775,7 +776,10 @@ def run_h3b(args) -> dict | None:
         "config": {
             "workload": f"{cfg.name} DiT block forward, packed Ulysses SP{world}",
             "seq": cfg.seq, "video_tokens": cfg.video_tokens, "audio_tokens": cfg.audio_tokens,
-            "dim": cfg.dim, "heads": cfg.heads, "head_dim": cfg.head_dim, "ffn": f"{cfg.ffn_inner} gelu-tanh" + ("" if args.no_gemm_epilogue else " (in the GEMM epilogue)"),
+            "dim": cfg.dim, "heads": cfg.heads, "head_dim": cfg.head_dim,
+            "ffn": f"{cfg.ffn_inner} gelu-tanh" + ("" if args.no_gemm_epilogue else
+                                                   " (h3b GEMM epilogues: GELU in the projection, the gated "
+                                                   "residual in the output projection)"),
             "rotary_dim": cfg.rotary_dim, "rows_per_rank": rows, "heads_per_rank": hl,
             "parallelism": f"ulysses_sp{world}",
             "qkv_projection": ("h3b tcgen05 GEMM with QK-norm + RoPE + pack (+ QKV exchange at p2p) in its epilogue"
@@ -834,6 +838,57 @@ def run_h3b(args) -> dict | None:
         "clocks": clocks,
     }
     return result
+
+
+def gemm_ab(cfg, steps: int, flush) -> dict:
+    """The block's GEMMs at the N=1 shape (S rows), this package's tcgen05 GEMM with its
+    fused epilogue against cuBLAS (and cuBLASLt's bias+GELU epilogue for the FFN
+    projection), in one process. TFLOP/s = 2 S K N / time."""
+
+    import torch.nn.functional as F
+
+    from h3_flash_b200.runtime.kernels.fusions import fused_linear, fused_qkv_gemm_pack
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    s, d, f = cfg.seq, cfg.dim, cfg.ffn_inner
+    rnd = lambda *shape, std=1.0: (torch.randn(*shape, device="cuda", generator=g) * std).to(torch.bfloat16)  # noqa: E731
+    x, h = rnd(s, d), rnd(s, f)
+    out = {}
+
+    def entry(name, k, n, arms):
+        flop = 2.0 * s * k * n
+        row = {"shape": f"[{s}, {k}] x [{k}, {n}]"}
+        for arm, fn in arms.items():
+            ms = _timed(fn, steps, 3, flush)
+            row[arm] = {"ms": round(ms, 4), "tflops": round(flop / (ms * 1e-3) / 1e12, 1)}
+        out[name] = row
+
+    w_qkv, b_qkv = rnd(3 * d, d, std=0.02), rnd(3 * d, std=0.02)
+    norm_w = torch.ones(cfg.head_dim, device="cuda", dtype=torch.bfloat16)
+    from h3_flash_b200.workloads import positions, rope_tables
+
+    cos, sin = (t.cuda() for t in rope_tables(positions(cfg), cfg.rotary_dim, cfg.theta))
+    send = torch.empty((1, s, cfg.heads, 3 * cfg.head_dim), device="cuda", dtype=torch.bfloat16)
+    entry("qkv_projection", d, 3 * d, {
+        "h3b_gemm_qknorm_rope_pack": lambda: fused_qkv_gemm_pack(x, w_qkv, b_qkv, norm_w, norm_w, cos, sin,
+                                                                  cfg.heads, 1, cfg.eps, cfg.eps, out=send),
+        "cublas_linear": lambda: F.linear(x, w_qkv, b_qkv)})
+    w_up, b_up = rnd(f, d, std=0.02), rnd(f, std=0.02)
+    up_out = torch.empty((s, f), device="cuda", dtype=torch.bfloat16)
+    entry("ffn_up_gelu_tanh", d, f, {
+        "h3b_gemm_gelu_epilogue": lambda: fused_linear(x, w_up, b_up, "gelu-tanh", out=up_out),
+        "cublaslt_gelu_epilogue": lambda: torch._addmm_activation(b_up, x, w_up.t(), use_gelu=True),
+        "cublas_linear_then_torch_gelu": lambda: F.gelu(F.linear(x, w_up, b_up), approximate="tanh")})
+    w_down, b_down = rnd(d, f, std=0.02), rnd(d, std=0.02)
+    down_out = torch.empty((s, d), device="cuda", dtype=torch.bfloat16)
+    entry("ffn_down", f, d, {"h3b_gemm": lambda: fused_linear(h, w_down, b_down, out=down_out),
+                             "cublas_linear": lambda: F.linear(h, w_down, b_down)})
+    w_o, b_o = rnd(d, d, std=0.02), rnd(d, std=0.02)
+    entry("attention_out", d, d, {"h3b_gemm": lambda: fused_linear(x, w_o, b_o, out=down_out),
+                                  "cublas_linear": lambda: F.linear(x, w_o, b_o)})
+    del x, h, send, up_out
+    torch.cuda.empty_cache()
+    return out
 
 
 def side_block(stack, config: str, steps: int, flush) -> dict:
@@ -977,6 +1032,20 @@ def profile_kernel(args) -> None:
         out = torch.empty((world, rows, args.heads_per_rank, 3 * cfg.head_dim), device="cuda", dtype=torch.bfloat16)
         for _ in range(args.warmup + args.steps):
             fused_qkv_gemm_pack(x, w, b, norm, norm, cos, sin, cfg.heads, world, cfg.eps, cfg.eps, out=out)
+    elif args.profile_kernel == "gemm_gelu":
+        # The FFN projection with GELU-tanh in the GEMM epilogue, one rank's rows at
+        # the SP layout given by --heads-per-rank (24: the N=1 shape).
+        from h3_flash_b200.runtime.kernels.fusions import fused_linear
+
+        world = cfg.heads // args.heads_per_rank
+        rows = cfg.seq // world
+        g = torch.Generator(device="cuda").manual_seed(0)
+        x = torch.randn(rows, cfg.dim, device="cuda", generator=g).to(torch.bfloat16)
+        w = (0.02 * torch.randn(cfg.ffn_inner, cfg.dim, device="cuda", generator=g)).to(torch.bfloat16)
+        b = (0.02 * torch.randn(cfg.ffn_inner, device="cuda", generator=g)).to(torch.bfloat16)
+        out = torch.empty((rows, cfg.ffn_inner), device="cuda", dtype=torch.bfloat16)
+        for _ in range(args.warmup + args.steps):
+            fused_linear(x, w, b, "gelu-tanh", out=out)
     torch.cuda.synchronize()
     from h3_flash_b200 import _lib
 
@@ -1178,7 +1247,8 @@ def main() -> int:
                         help="packed-Ulysses row exchange for N>1: NCCL all-to-all or NVLink peer stores")
     parser.add_argument("--no-cpu-baseline", action="store_true")
     parser.add_argument("--no-gemm-epilogue", action="store_true",
-                        help="GELU as a separate h3b kernel instead of inside the FFN GEMM")
+                        help="cuBLAS FFN/out projections with the GELU and the gated residual as separate h3b "
+                             "kernels, instead of the h3b GEMM epilogues")
     parser.add_argument("--transformer-bench", action="store_true",
                         help="time the whole H3 transformer per request (f1/f2 mechanisms) instead")
     parser.add_argument("--layers", type=int, default=2, help="blocks in --transformer-bench")
@@ -1194,7 +1264,7 @@ def main() -> int:
     parser.add_argument("--no-eager-baseline", action="store_true",
                         help="skip timing the unfused torch block at N=1")
     parser.add_argument("--sweep", choices=["elementwise"], help="print the config-2 kernel sweep instead")
-    parser.add_argument("--profile-kernel", choices=["attention", "elementwise", "qkv_gemm"],
+    parser.add_argument("--profile-kernel", choices=["attention", "elementwise", "qkv_gemm", "gemm_gelu"],
                         help="launch one kernel family for an ncu capture")
     parser.add_argument("--heads-per-rank", type=int, default=3)
     parser.add_argument("--exchange-bench", action="store_true",

@@ -21,7 +21,7 @@ H3B_OK = 0
 H3B_ERR_VALUE = 1
 H3B_ERR_CUDA = 2
 H3B_ERR_UNSUPPORTED = 3
-ABI_VERSION = 6
+ABI_VERSION = 7
 IPC_HANDLE_BYTES = 64
 
 _p = ctypes.c_void_p
@@ -55,6 +55,10 @@ SIGNATURES: dict[str, list[Any]] = {
                           _i64, _f32, _f32, _p],
     "h3b_qkv_gemm_pack_p2p": [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p,
                               _i64, _i64, _i64, _f32, _f32, _p],
+    "h3b_gemm": [_p, _i64, _p, _i64, _i64, _i64, _p, _i64, _p, _i64, _p],
+    "h3b_gemm_swiglu": [_p, _i64, _p, _i64, _i64, _i64, _p, _i64, _p, _p],
+    "h3b_gemm_gated_residual": [_p, _i64, _p, _i64, _i64, _i64, _p, _i64, _p, _p, _i64, _p, _i64, _p, _i64,
+                                _p],
     "h3b_attention_p2p": [_p, _p, _i64, _i64, _p, _i64, _i64, _f32, _p, _i64, _p],
     "h3b_peer_barrier": [_p, _i64, _i64, _p],
     "h3b_ipc_handle": [_p, _p, ctypes.POINTER(_i64)],

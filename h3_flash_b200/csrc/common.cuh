@@ -177,4 +177,33 @@ inline int num_sms() {
   return sms;
 }
 
+// ---- activations (fp32 in, fp32 out; MUFU ex2 / rcp) ---------------------
+
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float rcpf(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// silu(g) = g * sigmoid(g) = g / (1 + 2^(-g log2 e)): two MUFU ops, relative
+// error a few fp32 ulps (results below 2^-126 flush to zero).
+__device__ __forceinline__ float silu(float g) {
+  return g * rcpf(1.f + ex2f(g * -1.4426950408889634f));
+}
+
+// gelu_tanh(x) = 0.5 x (1 + tanh(u)) = x * sigmoid(2u), u = sqrt(2/pi)(x + 0.044715 x^3),
+// i.e. x / (1 + 2^(x (c1 + c2 x^2))) with c1 = -2 sqrt(2/pi) log2(e), c2 = c1 * 0.044715.
+// The sigmoid form has no cancellation for negative x; two MUFU ops per element.
+__device__ __forceinline__ float gelu_tanh(float x) {
+  const float c1 = -2.f * 0.7978845608028654f * 1.4426950408889634f;
+  const float c2 = c1 * 0.044715f;
+  const float e = ex2f(x * fmaf(c2, x * x, c1));
+  return x * rcpf(1.f + e);
+}
+
 }  // namespace h3b

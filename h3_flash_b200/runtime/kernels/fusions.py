@@ -289,3 +289,118 @@ def fused_qkv_gemm_pack(x, weight, bias, q_weight, k_weight, cos, sin, heads, wo
          ptr(sin32) if sin32 is not None else None, heads, 128, rotary_dim, float(q_eps),
          float(k_eps), stream_of(x))
     return out
+
+
+# ---------------------------------------------------------------------------
+# GEMMs with the activation in the epilogue (h3b tcgen05 GEMM)
+# ---------------------------------------------------------------------------
+
+_ACTIVATIONS = {"none": 0, "gelu-tanh": 1}
+
+
+def gemm_supported(x: torch.Tensor, weight: torch.Tensor, n_multiple: int = 256) -> bool:
+    """Whether the h3b GEMM serves ``x @ weight.T``: bf16 CUDA tensors, a contiguous
+    [n, dim] weight, dim % 64 == 0 and n % ``n_multiple`` == 0."""
+
+    return (x.is_cuda and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16
+            and weight.dim() == 2 and weight.is_contiguous() and x.shape[-1] == weight.shape[1]
+            and weight.shape[1] % 64 == 0 and weight.shape[0] % n_multiple == 0)
+
+
+def _gemm_input(op: str, x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None):
+    require_cuda(op, x, weight)
+    require_bf16(op, x, weight)
+    x2d = x.reshape(-1, x.shape[-1])
+    if x2d.stride(-1) != 1 or x2d.stride(0) % 8 or x2d.data_ptr() % 16:
+        x2d = x2d.contiguous()
+    if bias is not None:
+        require_bf16(op, bias)
+        bias = bias.contiguous()
+    return x2d, weight.contiguous(), bias
+
+
+def fused_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None = None,
+                 activation: str = "none", out: torch.Tensor | None = None) -> torch.Tensor:
+    """``act(x @ weight.T + bias)`` as one h3b tcgen05 GEMM with the bias and the
+    activation in its epilogue: the [rows, n] pre-activation is never stored, and it is
+    not rounded to bf16 before the activation. ``activation``: "none" or "gelu-tanh"
+    (the GELU-tanh FFN projection of src/h3_flash/runtime/kernels/transformer.py:121-122).
+    x [..., dim], weight [n, dim] (nn.Linear layout), bias [n] or None."""
+
+    op = "fused_linear"
+    if activation not in _ACTIVATIONS:
+        raise ValueError(f"{op}: activation must be one of {sorted(_ACTIVATIONS)}")
+    x2d, weight, bias = _gemm_input(op, x, weight, bias)
+    rows, n = x2d.shape[0], weight.shape[0]
+    if out is None:
+        out = torch.empty((rows, n), dtype=x.dtype, device=x.device)
+    if rows:
+        call("h3b_gemm", ptr(out), out.stride(0), ptr(x2d), rows, x2d.shape[1], x2d.stride(0), ptr(weight), n,
+             ptr(bias) if bias is not None else None, _ACTIVATIONS[activation], stream_of(x))
+    return out.view(*x.shape[:-1], n)
+
+
+def interleave_swiglu(weight: torch.Tensor, bias: torch.Tensor | None = None):
+    """The SwiGLU projection's weight [2n, dim] (value rows, then gate rows) and bias
+    [2n] reordered for ``fused_linear_swiglu``: blocks of 128 value rows alternate with
+    the matching 128 gate rows. Needs n % 128 == 0."""
+
+    two_n, dim = weight.shape
+    n = two_n // 2
+    if two_n % 2 or n % 128:
+        raise ValueError(f"interleave_swiglu: projection width {two_n} is not 2 x a multiple of 128")
+    value, gate = weight.view(2, n // 128, 128, dim).unbind(0)
+    w = torch.stack([value, gate], dim=1).reshape(two_n, dim).contiguous()
+    b = None
+    if bias is not None:
+        bv, bg = bias.view(2, n // 128, 128).unbind(0)
+        b = torch.stack([bv, bg], dim=1).reshape(two_n).contiguous()
+    return w, b
+
+
+def fused_linear_swiglu(x: torch.Tensor, weight_interleaved: torch.Tensor,
+                        bias_interleaved: torch.Tensor | None = None,
+                        out: torch.Tensor | None = None) -> torch.Tensor:
+    """``fused_swiglu(x @ W.T + b)`` as one h3b GEMM (value * silu(gate) in its
+    epilogue; src/h3_flash/runtime/kernels/transformer.py:112-115, fusions.py:251-265),
+    with W and b given by ``interleave_swiglu``. Returns [..., n]."""
+
+    op = "fused_linear_swiglu"
+    x2d, w, b = _gemm_input(op, x, weight_interleaved, bias_interleaved)
+    rows, n = x2d.shape[0], w.shape[0] // 2
+    if out is None:
+        out = torch.empty((rows, n), dtype=x.dtype, device=x.device)
+    if rows:
+        call("h3b_gemm_swiglu", ptr(out), out.stride(0), ptr(x2d), rows, x2d.shape[1], x2d.stride(0), ptr(w), n,
+             ptr(b) if b is not None else None, stream_of(x))
+    return out.view(*x.shape[:-1], n)
+
+
+def fused_linear_gated_residual(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None,
+                                residual: torch.Tensor, gate: torch.Tensor, index=None,
+                                out: torch.Tensor | None = None) -> torch.Tensor:
+    """``residual + gate[index] * (x @ weight.T + bias)`` as one h3b GEMM: the block's
+    closing gated residual (src/h3_flash/runtime/kernels/transformer.py:123-126) in the
+    epilogue of the FFN output projection (:120), the projection kept in fp32 up to the
+    product. residual [..., n] like the output; gate [n_table, n] (rows picked by
+    ``index[row % len(index)]``, all rows the first table row when ``index`` is None)."""
+
+    op = "fused_linear_gated_residual"
+    x2d, weight, bias = _gemm_input(op, x, weight, bias)
+    require_cuda(op, residual, gate)
+    require_bf16(op, residual, gate)
+    rows, n = x2d.shape[0], weight.shape[0]
+    res = residual.reshape(-1, n)
+    if res.shape[0] != rows:
+        raise ValueError(f"{op}: residual has {res.shape[0]} rows, x has {rows}")
+    if res.stride(-1) != 1 or res.stride(0) % 8 or res.data_ptr() % 16:
+        res = res.contiguous()
+    table, table_stride = table_rows(gate)
+    idx = index64(index, x.device)
+    if out is None:
+        out = torch.empty((rows, n), dtype=x.dtype, device=x.device)
+    if rows:
+        call("h3b_gemm_gated_residual", ptr(out), out.stride(0), ptr(x2d), rows, x2d.shape[1], x2d.stride(0),
+             ptr(weight), n, ptr(bias) if bias is not None else None, ptr(res), res.stride(0), ptr(table),
+             table_stride, ptr(idx), idx.numel(), stream_of(x))
+    return out.view(*residual.shape[:-1], n)

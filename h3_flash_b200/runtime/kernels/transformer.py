@@ -26,9 +26,14 @@ from .fusions import (
     HAVE_CUDA_KERNELS,
     fused_gated_residual,
     fused_gelu_tanh,
+    fused_linear,
+    fused_linear_gated_residual,
+    fused_linear_swiglu,
     fused_residual_gate_rmsnorm_modulate,
     fused_rmsnorm_modulate,
     fused_swiglu,
+    gemm_supported,
+    interleave_swiglu,
 )
 
 
@@ -71,45 +76,74 @@ def _eager_activation(kind: str, projected: torch.Tensor) -> torch.Tensor:
     return torch.nn.functional.gelu(projected, approximate="tanh")
 
 
-def _gelu_epilogue_supported(proj: Any, x: torch.Tensor) -> bool:
-    """cuBLASLt's bias+GELU(tanh) epilogue serves a 2-D bf16/fp16 CUDA GEMM with a bias."""
+def _swiglu_weights(act_layer: Any) -> tuple[torch.Tensor, torch.Tensor | None]:
+    """The SwiGLU projection's weight and bias interleaved for ``fused_linear_swiglu``,
+    cached on the layer and rebuilt when the weight or bias changes (in place or by
+    reassignment)."""
 
-    weight, bias = getattr(proj, "weight", None), getattr(proj, "bias", None)
-    return (hasattr(torch, "_addmm_activation") and x.is_cuda and bias is not None and weight is not None
-            and x.dtype in (torch.bfloat16, torch.float16) and weight.dtype == x.dtype
-            and bias.dtype == x.dtype and weight.is_contiguous() and bias.is_contiguous()
-            and x.stride(-1) == 1 and x.numel() > 0)
+    proj = act_layer.proj
+    key = tuple((t.data_ptr(), t._version) if t is not None else None for t in (proj.weight, proj.bias))
+    cached = getattr(act_layer, "_h3b_swiglu_interleaved", None)
+    if cached is None or cached[0] != key:
+        with torch.no_grad():
+            cached = (key, *interleave_swiglu(proj.weight, proj.bias))
+        act_layer._h3b_swiglu_interleaved = cached
+    return cached[1], cached[2]
 
 
-def feed_forward(ff: Any, normed: torch.Tensor, fuse_activation: bool, gate: dict | None = None,
-                 gemm_epilogue: bool = False) -> torch.Tensor:
-    """``gemm_epilogue``: a GELU-tanh FFN runs its activation inside the projection GEMM
-    (cuBLASLt bias+GELU epilogue), so the [rows, inner] pre-activation is never stored
-    and the pre-activation is not rounded to bf16 before the GELU."""
+def _activated(ff: Any, normed: torch.Tensor, fuse_activation: bool, gate: dict | None,
+               gemm_epilogue: bool) -> torch.Tensor | None:
+    """The FFN's activated hidden [..., inner] through this package's kernels, or None
+    for an FFN this package does not fuse. With ``gemm_epilogue`` the GELU-tanh or
+    SwiGLU runs inside the projection GEMM (the h3b tcgen05 GEMM with the bias and the
+    activation in its epilogue: the [rows, inner] pre-activation is never stored nor
+    rounded to bf16 before the activation); shapes that GEMM does not serve, and
+    ``gemm_epilogue=False``, take cuBLAS and then the h3b activation kernel."""
 
     act_layer, _, output_projection = ff.net
     kind = _activation_kind(act_layer, output_projection) if fuse_activation else None
     if kind is None:
+        return None
+    proj = act_layer.proj
+    if gemm_epilogue and gemm_supported(normed, proj.weight):
         with TIMER.section("gemm"):
-            return ff(normed)
-    if kind == "gelu_tanh" and gemm_epilogue and _gelu_epilogue_supported(act_layer.proj, normed):
-        proj = act_layer.proj
-        with TIMER.section("gemm"):
-            flat = normed.reshape(-1, normed.shape[-1])
-            activated = torch._addmm_activation(proj.bias, flat, proj.weight.t(), use_gelu=True)
-            activated = activated.view(*normed.shape[:-1], proj.out_features)
-        if gate is not None and "gelu_tanh_epilogue" not in gate:
-            gate["gelu_tanh_epilogue"] = _error_metrics(activated, _eager_activation(kind, proj(normed)))
-        with TIMER.section("gemm"):
-            return output_projection(activated)
+            if kind == "gelu_tanh":
+                activated = fused_linear(normed, proj.weight, proj.bias, "gelu-tanh")
+            else:
+                activated = fused_linear_swiglu(normed, *_swiglu_weights(act_layer))
+        name = f"{kind}_epilogue"
+        if gate is not None and name not in gate:
+            gate[name] = _error_metrics(activated, _eager_activation(kind, proj(normed)))
+        return activated
     with TIMER.section("gemm"):
-        projected = act_layer.proj(normed)
+        projected = proj(normed)
     with TIMER.section("elementwise"):
         activated = fused_swiglu(projected) if kind == "swiglu" else fused_gelu_tanh(projected)
     if gate is not None and kind not in gate:
         gate[kind] = _error_metrics(activated, _eager_activation(kind, projected))
+    return activated
+
+
+def linear(layer: Any, x: torch.Tensor) -> torch.Tensor:
+    """``layer(x)`` for an nn.Linear: the h3b tcgen05 GEMM (bias in its epilogue) where it
+    serves the shape, else the layer itself (cuBLAS)."""
+
+    if isinstance(layer, torch.nn.Linear) and gemm_supported(x, layer.weight):
+        return fused_linear(x, layer.weight, layer.bias)
+    return layer(x)
+
+
+def feed_forward(ff: Any, normed: torch.Tensor, fuse_activation: bool, gate: dict | None = None,
+                 gemm_epilogue: bool = False) -> torch.Tensor:
+    """The FFN of one block (``block.ff``) with its activation fused as ``_activated``
+    describes; the output projection on the h3b GEMM with ``gemm_epilogue``."""
+
+    activated = _activated(ff, normed, fuse_activation, gate, gemm_epilogue)
     with TIMER.section("gemm"):
-        return output_projection(activated)
+        if activated is None:
+            return ff(normed)
+        output_projection = ff.net[2]
+        return linear(output_projection, activated) if gemm_epilogue else output_projection(activated)
 
 
 def fused_block_forward(block: Any, hidden_states: torch.Tensor, temb: Any, adaln_indices: torch.Tensor,
@@ -149,7 +183,19 @@ def fused_block_forward(block: Any, hidden_states: torch.Tensor, temb: Any, adal
         hidden_states = hidden_states + gate_msa.index_select(0, adaln_indices) * attention_output
         normed = block.norm2(hidden_states)
         normed = normed * (1.0 + scale_mlp.index_select(0, adaln_indices)) + shift_mlp.index_select(0, adaln_indices)
-    feed_forward_output = feed_forward(block.ff, normed, swiglu, gate, gemm_epilogue)
+    if modulate and gemm_epilogue:
+        # The closing gated residual in the epilogue of the FFN output projection.
+        activated = _activated(block.ff, normed, swiglu, gate, gemm_epilogue)
+        output_projection = block.ff.net[2] if activated is not None else None
+        if output_projection is not None and isinstance(output_projection, torch.nn.Linear) and \
+                gemm_supported(activated, output_projection.weight):
+            with TIMER.section("gemm"):
+                return fused_linear_gated_residual(activated, output_projection.weight, output_projection.bias,
+                                                   hidden_states, gate_mlp, adaln_indices)
+        with TIMER.section("gemm"):
+            feed_forward_output = block.ff(normed) if activated is None else linear(output_projection, activated)
+    else:
+        feed_forward_output = feed_forward(block.ff, normed, swiglu, gate, gemm_epilogue)
     if modulate:
         with TIMER.section("elementwise"):
             return fused_gated_residual(hidden_states, feed_forward_output, gate_mlp, adaln_indices)
@@ -191,9 +237,10 @@ def install_transformer_fusions(transformer: Any, *, modulate: bool = True, swig
                                 qknorm_rope: bool = True, gemm_epilogue: bool = True,
                                 gemm_pack: bool = True) -> dict[str, Any]:
     """kernels/transformer.py:207-228. ``swiglu`` toggles the fused FFN activation
-    (SwiGLU for H3, GELU-tanh for the BASELINE block). ``gemm_epilogue`` runs a
-    GELU-tanh activation inside the FFN projection GEMM (cuBLASLt epilogue) instead
-    of the h3b elementwise kernel after it; SwiGLU always uses the h3b kernel.
+    (SwiGLU for H3, GELU-tanh for the BASELINE block). ``gemm_epilogue`` runs the
+    activation inside the FFN projection GEMM (the h3b tcgen05 GEMM's epilogue; SwiGLU
+    on a weight whose value and gate rows are interleaved once and cached) instead of
+    the h3b elementwise kernel after a cuBLAS GEMM.
     ``gemm_pack`` runs the QKV projection, QK-norm + RoPE and the pack as one
     h3b tcgen05 GEMM where the shapes allow it."""
 

@@ -231,6 +231,15 @@ def _norm_params(norm: Any) -> tuple[torch.Tensor, float] | None:
     return weight, float(eps)
 
 
+def _out_projection(attention: Any, output: torch.Tensor) -> torch.Tensor:
+    """``attention.to_out[0](output)`` on the h3b tcgen05 GEMM where it serves the shape
+    (bias in the epilogue), else the layer itself (cuBLAS)."""
+
+    from ..kernels.transformer import linear
+
+    return linear(attention.to_out[0], output)
+
+
 def ulysses_attention_forward(attention: Any, hidden_states: torch.Tensor, rotary_emb: Any = None,
                               attention_mask: Any = None, *, runtime: PackedUlyssesRuntime | None = None,
                               fused_qknorm_rope: bool = True, gemm_pack: bool = True) -> torch.Tensor:
@@ -265,7 +274,7 @@ def ulysses_attention_forward(attention: Any, hidden_states: torch.Tensor, rotar
         output = output.reshape(batch, rows_local, heads * head_dim).type_as(hidden_states)
         runtime.attention_calls += 1
         with TIMER.section("gemm"):
-            return attention.to_out[1](attention.to_out[0](output))
+            return attention.to_out[1](_out_projection(attention, output))
     if use_gemm:
         with TIMER.section("qkv_gemm_pack"):
             send = fused_qkv_gemm_pack(x2d, stacked[0], stacked[1], norm_q[0], norm_k[0], cos, sin,
@@ -300,7 +309,7 @@ def ulysses_attention_forward(attention: Any, hidden_states: torch.Tensor, rotar
     if runtime is not None:
         runtime.attention_calls += 1
     with TIMER.section("gemm"):
-        return attention.to_out[1](attention.to_out[0](output))
+        return attention.to_out[1](_out_projection(attention, output))
 
 
 def _p2p_supported(head_dim: int, cos: Any) -> bool:

@@ -30,7 +30,7 @@ typedef struct CUstream_st* h3b_stream_t; /* == cudaStream_t */
 #define H3B_ERR_CUDA 2        /* CUDA launch or driver error: RuntimeError         */
 #define H3B_ERR_UNSUPPORTED 3 /* valid input this build does not handle: RuntimeError */
 
-#define H3B_ABI_VERSION 6
+#define H3B_ABI_VERSION 7
 
 int h3b_abi_version(void);
 /* Kernels launched through this library by this process (all devices and host
@@ -148,6 +148,43 @@ int h3b_qkv_gemm_pack(void* send, int64_t world, const void* x, int64_t rows, in
                       const void* q_weight, const void* k_weight, const float* cos,
                       const float* sin, int64_t heads, int64_t head_dim, int64_t rotary_dim,
                       float q_eps, float k_eps, h3b_stream_t stream);
+
+/* out[row, :n] = act(x W^T + bias): x [rows, dim] (row stride x_row_stride),
+ * W [n, dim] row-major (nn.Linear layout), bias [n] or NULL, out row stride
+ * out_row_stride; bf16 in/out, fp32 accumulation, one rounding at the store.
+ * activation 0: none; 1: GELU-tanh (x * sigmoid(2u), u = sqrt(2/pi)(x +
+ * 0.044715 x^3)). Needs dim % 64 == 0 and n % 256 == 0 (else H3B_ERR_UNSUPPORTED).
+ * replaces the FFN projection + activation of block.ff  kernels/transformer.py:121-122
+ *          (and any plain Linear: to_out, the FFN output projection) */
+int h3b_gemm(void* out, int64_t out_row_stride, const void* x, int64_t rows, int64_t dim,
+             int64_t x_row_stride, const void* w, int64_t n, const void* bias,
+             int64_t activation, h3b_stream_t stream);
+
+/* out[row, :n] = residual[row] + gate[index[row % n_index]] * (x W^T + bias)[row]:
+ * the block's closing gated residual fused into the FFN output projection (or any
+ * projection followed by a gated residual). residual [rows, n] and the gate table
+ * [n_table, n] by row strides; the projection stays in fp32 up to the product.
+ * Needs dim % 64 == 0 and n % 256 == 0.
+ * replaces output_projection + hidden + gate_mlp[idx] * ffn
+ *          kernels/transformer.py:120, :123-126 */
+int h3b_gemm_gated_residual(void* out, int64_t out_row_stride, const void* x, int64_t rows,
+                            int64_t dim, int64_t x_row_stride, const void* w, int64_t n,
+                            const void* bias, const void* residual,
+                            int64_t residual_row_stride, const void* gate,
+                            int64_t gate_row_stride, const int64_t* index, int64_t n_index,
+                            h3b_stream_t stream);
+
+/* out[row, :n_out] = value * silu(gate) of the SwiGLU projection, computed from an
+ * interleaved weight: rows [256b, 256b+128) of w_interleaved are value rows
+ * [128b, 128b+128) of the projection, rows [256b+128, 256b+256) the gate rows
+ * n_out + [128b, 128b+128); bias_interleaved [2 n_out] in the same order, or NULL.
+ * The projection stays in fp32 up to the product (one rounding, at the store).
+ * Needs dim % 64 == 0 and n_out % 128 == 0.
+ * replaces swiglu_layer.proj + fused_swiglu  kernels/transformer.py:112-115,
+ *          fusions.py:251-265 */
+int h3b_gemm_swiglu(void* out, int64_t out_row_stride, const void* x, int64_t rows,
+                    int64_t dim, int64_t x_row_stride, const void* w_interleaved,
+                    int64_t n_out, const void* bias_interleaved, h3b_stream_t stream);
 
 /* out[dst, row, h, :] = (q|k|v)[row, dst*hl + h, :], out is [world, rows, hl, 3*head_dim].
  * q/k/v are [rows, heads, head_dim] with element strides (row, head), last dim contiguous.

@@ -88,7 +88,7 @@ def test_block_is_deterministic_and_reuses_qkv_cache():
 
 
 def test_gelu_in_the_gemm_epilogue_is_tanh_gelu():
-    """The FFN projection with GELU in its epilogue (cuBLASLt) vs the fp32 GELU-tanh of the
+    """The FFN projection with GELU in its epilogue (h3b GEMM) vs the fp32 GELU-tanh of the
     fp32 projection: within the bf16 bar, no worse than the unfused GEMM + h3b GELU, and
     tanh-GELU rather than erf-GELU where the two differ by many bf16 spacings (x near -3)."""
 
@@ -102,9 +102,11 @@ def test_gelu_in_the_gemm_epilogue_is_tanh_gelu():
         ff.net[0].proj.bias.normal_(0.0, 0.5)
         x = torch.randn(1, 700, 512, device="cuda").to(torch.bfloat16)
         gate = {}
-        # the activation itself: the same epilogue call feed_forward makes
+        # the activation itself: the same h3b GEMM epilogue call feed_forward makes
+        from h3_flash_b200.runtime.kernels.fusions import fused_linear
+
         proj = ff.net[0].proj
-        fused = torch._addmm_activation(proj.bias, x[0], proj.weight.t(), use_gelu=True).float()
+        fused = fused_linear(x[0], proj.weight, proj.bias, "gelu-tanh").float()
         unfused = torch.nn.functional.gelu(proj(x[0]).float(), approximate="tanh").to(torch.bfloat16).float()
         pre = x[0].float() @ proj.weight.float().t() + proj.bias.float()
         tanh_ref = torch.nn.functional.gelu(pre, approximate="tanh")
