@@ -757,6 +757,16 @@ def run_h3b(args) -> dict | None:
                                                   "move inside the attention kernel")
     a2a_ms = _max_over_ranks(sum(sum(sections.get(k, [0.0])) for k in a2a_keys) / max(args.steps, 1), world)
     sections_total = {k: round(sum(v) / args.steps, 4) for k, v in sections.items()}
+    # The exchange's own NVLink rate: with the default path the transfers run inside the
+    # QKV GEMM and attention kernels, so time the same rows moved by the standalone peer
+    # kernels (and by NCCL) on this rank's shape.
+    exchange = None
+    if world > 1 and not args.no_exchange_roofline:
+        if runtime is not None and runtime.peer is not None:
+            runtime.peer.close()
+            runtime.peer = None
+        torch.cuda.empty_cache()
+        exchange = exchange_timings(args.config, rank, world, min(args.steps, 10), 3)
 
     if rank != 0:
         return None
@@ -830,6 +840,7 @@ def run_h3b(args) -> dict | None:
                                   "frac": round(a2a_bytes / (a2a_ms * 1e-3) / 1e9 / NVLINK_PEER_GBS, 4)
                                   if a2a_ms and a2a_bytes else None},
         },
+        "exchange_standalone": exchange,
         "sections_ms_per_step": sections_total,
         "gpu_reference_block": reference,
         "gpu_eager_baseline": eager,
@@ -837,6 +848,22 @@ def run_h3b(args) -> dict | None:
         "gpu_launches": launches,
         "clocks": clocks,
     }
+    if exchange is not None:
+        ms = exchange["ms"]
+        moving = (ms["pack_p2p_and_barrier"] - ms["barrier"]) + (ms["scatter_p2p_and_barrier"] - ms["barrier"])
+        sent = (exchange["remote_mb_per_rank"]["qkv"] + exchange["remote_mb_per_rank"]["output"]) * 1e6
+        gbs = sent / (moving * 1e-3) / 1e9 if moving > 0 else None
+        result["rooflines"]["all_to_all_nvlink"]["standalone"] = {
+            "what": "the QKV rows (pack kernel storing at the owners) and the output rows (scatter kernel) "
+                    "of one block moved by the standalone peer kernels, barrier time excluded; the default "
+                    "path moves the same rows inside the QKV GEMM and attention kernels",
+            "bytes_sent_per_gpu": sent, "ms": round(moving, 4),
+            "achieved_gbs": round(gbs, 1) if gbs else None,
+            "frac_of_measured_peer_copy": round(gbs / NVLINK_PEER_GBS, 4) if gbs else None,
+            "frac_of_900_nominal": round(gbs / 900.0, 4) if gbs else None,
+            "nccl_all_to_all_ms": {"qkv": ms["nccl_qkv_all_to_all"],
+                                   "output_and_merge": ms["nccl_output_all_to_all_and_merge"]},
+        }
     return result
 
 
@@ -1059,6 +1086,16 @@ def exchange_bench(args) -> dict | None:
     (N>1 under torchrun): the peer-store path (pack to the owners, barrier, scatter)
     against NCCL all-to-all of the same rows. CUDA events, max over ranks."""
 
+    rank, world, _ = _dist_setup(args.gpus)
+    if world < 2:
+        raise SystemExit("--exchange-bench needs N>1 (launch under torchrun)")
+    return exchange_timings(args.config, rank, world, args.steps, args.warmup)
+
+
+def exchange_timings(config: str, rank: int, world: int, steps: int, warmup: int) -> dict | None:
+    """The exchange operations of one block at ``config``'s shape on this rank's rows
+    (every rank calls it): collective, returns rank 0's line."""
+
     import torch.distributed as dist
 
     from h3_flash_b200.runtime.kernels.fusions import fused_qknorm_rope_pack
@@ -1070,10 +1107,7 @@ def exchange_bench(args) -> dict | None:
     from h3_flash_b200.runtime.parallel.peer_exchange import PeerExchange
     from h3_flash_b200.workloads import CONFIGS, split_sizes
 
-    rank, world, _ = _dist_setup(args.gpus)
-    if world < 2:
-        raise SystemExit("--exchange-bench needs N>1 (launch under torchrun)")
-    cfg = CONFIGS[args.config]
+    cfg = CONFIGS[config]
     heads, dim = cfg.heads, cfg.head_dim
     counts = split_sizes(cfg.seq, world)
     rows = counts[rank]
@@ -1091,17 +1125,17 @@ def exchange_bench(args) -> dict | None:
     send = fused_qknorm_rope_pack(q, k, v, weight, weight, cos, sin, world, cfg.eps, cfg.eps)
 
     def timed(fn) -> float:
-        for _ in range(args.warmup):
+        for _ in range(warmup):
             fn()
         torch.cuda.synchronize()
         dist.barrier()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
-        for _ in range(args.steps):
+        for _ in range(steps):
             fn()
         end.record()
         torch.cuda.synchronize()
-        return _max_over_ranks(start.elapsed_time(end) / args.steps, world)
+        return _max_over_ranks(start.elapsed_time(end) / steps, world)
 
     def pack_p2p():
         peer.pack(q, k, v, weight, weight, cos, sin, cfg.eps, cfg.eps, counts)
@@ -1123,10 +1157,12 @@ def exchange_bench(args) -> dict | None:
     qkv_remote = max(counts) * heads * 3 * dim * 2 * (world - 1) / world
     out_remote = cfg.seq * (heads // world) * dim * 2 * (world - 1) / world
     peer.close()
+    del send, out, qkv
+    torch.cuda.empty_cache()
     if rank != 0:
         return None
     return {
-        "exchange_bench": cfg.name, "n_gpus": world, "steps": args.steps,
+        "exchange_bench": cfg.name, "n_gpus": world, "steps": steps,
         "ms": {key: round(value, 4) for key, value in ms.items()},
         "remote_mb_per_rank": {"qkv": round(qkv_remote / 1e6, 2), "output": round(out_remote / 1e6, 2)},
         "peer_gbs": {
@@ -1259,6 +1295,8 @@ def main() -> int:
                         help="cuBLAS QKV projection + the h3b pack kernel instead of the fused h3b QKV GEMM")
     parser.add_argument("--no-reference-block", action="store_true",
                         help="skip timing the reference's own LOSSLESS GPU block (gpu_reference_block)")
+    parser.add_argument("--no-exchange-roofline", action="store_true",
+                        help="N>1: skip timing the exchange operations standalone (exchange_standalone)")
     parser.add_argument("--no-side-lines", action="store_true",
                         help="N=1: skip the attention A/B, the 768p-5s block and the elementwise sweep keys")
     parser.add_argument("--no-eager-baseline", action="store_true",
