@@ -707,6 +707,9 @@ def run_h3b(args) -> dict | None:
     if reference is not None and "ms_per_step" in reference:
         reference["h3b_speedup"] = round(reference["ms_per_step"] / _max_over_ranks(statistics.mean(step_ms), world), 4)
     side = {}
+    if world == 8 and not args.no_side_lines and args.config == "480p-5s":
+        side["block_768p_15s_sp8"] = sp_side_block(stack, runtime, "768p-15s", rank, world, min(args.steps, 3),
+                                                   flush)
     if world == 1 and not args.no_side_lines:
         side["attention_ab"] = attention_ab(cfg, min(args.steps, 10), flush)
         side["gemm_ab"] = gemm_ab(cfg, min(args.steps, 10), flush)
@@ -945,6 +948,43 @@ def side_block(stack, config: str, steps: int, flush) -> dict:
     return {"config": f"{cfg.name}: S={cfg.seq} ({cfg.video_tokens} video + {cfg.audio_tokens} audio), SP1",
             "ms_per_step": round(ms, 3), "steps": steps, "attention_ms": round(attn, 3),
             "attention_tflops": round(flop / (attn * 1e-3) / 1e12, 1)}
+
+
+def sp_side_block(stack, runtime, config: str, rank: int, world: int, steps: int, flush) -> dict:
+    """The installed packed-Ulysses block stack at another BASELINE shape over the same
+    ranks (every rank calls it; a new request, so the row counts are exchanged again):
+    ms per block forward (max over ranks) and the in-step attention rate."""
+
+    from h3_flash_b200.runtime.timing import TIMER
+    from h3_flash_b200.workloads import CONFIGS, adaln_indices, positions, rope_tables, split_bounds
+
+    cfg = CONFIGS[config]
+    start, stop = split_bounds(cfg.seq, world, rank)
+    g = torch.Generator().manual_seed(1 + start)
+    hidden = torch.randn(1, stop - start, cfg.dim, generator=g).to(torch.bfloat16).cuda()
+    idx = adaln_indices(cfg)[start:stop].cuda()
+    cos, sin = rope_tables(positions(cfg), cfg.rotary_dim, cfg.theta)
+    rotary = (cos[start:stop].cuda(), sin[start:stop].cuda())
+
+    def step():
+        with torch.no_grad():
+            return stack(hidden, None, idx, rotary)
+
+    runtime.begin_request()  # new row counts (and, p2p, buffers sized for them)
+    for _ in range(2):
+        step()
+    TIMER.reset()
+    TIMER.enabled = True
+    ms = _timed(step, steps, 0, flush)
+    TIMER.enabled = False
+    attn = statistics.mean(TIMER.milliseconds().get("attention", [float("nan")]))
+    flop = 4.0 * cfg.seq * cfg.seq * (cfg.heads // world) * cfg.head_dim
+    del hidden
+    torch.cuda.empty_cache()
+    return {"config": f"{cfg.name}: S={cfg.seq} ({cfg.video_tokens} video + {cfg.audio_tokens} audio), SP{world}",
+            "ms_per_step": round(_max_over_ranks(ms, world), 3), "steps": steps,
+            "attention_ms": round(_max_over_ranks(attn, world), 3),
+            "attention_tflops_per_gpu": round(flop / (_max_over_ranks(attn, world) * 1e-3) / 1e12, 1)}
 
 
 def flush_l2(buf: torch.Tensor) -> None:

@@ -21,7 +21,7 @@ H3B_OK = 0
 H3B_ERR_VALUE = 1
 H3B_ERR_CUDA = 2
 H3B_ERR_UNSUPPORTED = 3
-ABI_VERSION = 7
+ABI_VERSION = 8
 IPC_HANDLE_BYTES = 64
 
 _p = ctypes.c_void_p
@@ -52,9 +52,10 @@ SIGNATURES: dict[str, list[Any]] = {
                                  _p, _i64, _i64, _i64, _i64, _f32, _f32, _p],
     "h3b_scatter_heads_p2p": [_p, _p, _p, _i64, _i64, _i64, _i64, _p],
     "h3b_qkv_gemm_pack": [_p, _i64, _p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p, _i64, _i64,
-                          _i64, _f32, _f32, _p],
+                          _i64, _f32, _f32, _p, _i64, _p],
+    "h3b_qkv_gemm_pack_workspace_size": [_i64, _i64, ctypes.POINTER(_i64)],
     "h3b_qkv_gemm_pack_p2p": [_p, _i64, _i64, _i64, _p, _i64, _i64, _i64, _p, _p, _p, _p, _p, _p,
-                              _i64, _i64, _i64, _f32, _f32, _p],
+                              _i64, _i64, _i64, _f32, _f32, _p, _i64, _p],
     "h3b_gemm": [_p, _i64, _p, _i64, _i64, _i64, _p, _i64, _p, _i64, _p],
     "h3b_gemm_swiglu": [_p, _i64, _p, _i64, _i64, _i64, _p, _i64, _p, _p],
     "h3b_gemm_gated_residual": [_p, _i64, _p, _i64, _i64, _i64, _p, _i64, _p, _p, _i64, _p, _i64, _p, _i64,

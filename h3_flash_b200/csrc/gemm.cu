@@ -241,6 +241,26 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
       : "memory");
 }
 
+// 32 lanes x 16 consecutive 32-bit TMEM columns -> 16 registers per thread.
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+// After tcgen05.wait::ld: ties each loaded register to this point of the program, so
+// no use of it can be scheduled above the wait.
+template <int N>
+__device__ __forceinline__ void pin(uint32_t (&r)[N]) {
+#pragma unroll
+  for (int j = 0; j < N; ++j) asm volatile("" : "+r"(r[j]));
+}
+
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
@@ -314,42 +334,6 @@ __device__ __forceinline__ void load32(uint32_t taddr, float (&x)[32]) {
   for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(v[j]);
 }
 
-template <int ROT>
-__device__ __forceinline__ void norm_rope_row(float (&x)[kHeadDim],
-                                              const __nv_bfloat16* __restrict__ w,
-                                              const float* __restrict__ cos_row,
-                                              const float* __restrict__ sin_row, float eps) {
-  float ss = 0.f;
-#pragma unroll
-  for (int c = 0; c < kHeadDim; ++c) ss += x[c] * x[c];
-  const float r = rsqrtf(ss / (float)kHeadDim + eps);
-#pragma unroll
-  for (int c8 = 0; c8 < kHeadDim / 8; ++c8) {
-    const f8 wv = unpack8(ld_cached(w + 8 * c8));
-#pragma unroll
-    for (int j = 0; j < 8; ++j) x[8 * c8 + j] = x[8 * c8 + j] * r * wv.v[j];
-  }
-  if constexpr (ROT > 0) {
-    constexpr int kHalf = ROT / 2;
-#pragma unroll
-    for (int c4 = 0; c4 < kHalf / 4; ++c4) {
-      const float4 ca = __ldg(reinterpret_cast<const float4*>(cos_row) + c4);
-      const float4 sa = __ldg(reinterpret_cast<const float4*>(sin_row) + c4);
-      const float4 cb = __ldg(reinterpret_cast<const float4*>(cos_row + kHalf) + c4);
-      const float4 sb = __ldg(reinterpret_cast<const float4*>(sin_row + kHalf) + c4);
-      const float cav[4] = {ca.x, ca.y, ca.z, ca.w}, sav[4] = {sa.x, sa.y, sa.z, sa.w};
-      const float cbv[4] = {cb.x, cb.y, cb.z, cb.w}, sbv[4] = {sb.x, sb.y, sb.z, sb.w};
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int c = 4 * c4 + j;
-        const float a = x[c], b = x[c + kHalf];
-        x[c] = a * cav[j] + (-b) * sav[j];  // first half takes -partner
-        x[c + kHalf] = b * cbv[j] + a * sbv[j];
-      }
-    }
-  }
-}
-
 // QKV projection + QK-norm + RoPE + pack. A 256-column tile never straddles q, k
 // and v (H D is a multiple of 256) and holds two heads: segment h is head g0 + h,
 // so the RMSNorm sum and every RoPE partner are in the thread's own registers.
@@ -357,43 +341,155 @@ template <int ROT, class Dst>
 struct QkvEpi {
   static constexpr int kSegments = 2;
   static constexpr bool kStaged = Dst::kStaged;
+  static constexpr int kHalf = ROT / 2;
+  static_assert(kHalf % 16 == 0, "rotary width: a multiple of 32");
   const __nv_bfloat16* bias;  // [3 H D] or nullptr
   const __nv_bfloat16* wq;    // [D]
   const __nv_bfloat16* wk;    // [D]
-  const float* cos;           // [rows, ROT]
-  const float* sin;
+  const float4* tab;          // RoPE tables in the epilogue's layout (rope_tables_kernel)
+  int64_t tab_rows;
   float q_eps, k_eps;
   int heads;
   Dst dst;
 
+  // bias + accumulator for 8 columns starting at column c of the segment
+  __device__ __forceinline__ void biased8(const uint32_t* v, int col, float (&x)[8]) const {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] = __uint_as_float(v[j]);
+    if (bias != nullptr) {
+      const f8 bv = unpack8(ld_cached(bias + col));
+#pragma unroll
+      for (int j = 0; j < 8; ++j) x[j] += bv.v[j];
+    }
+  }
+
+  // RoPE table slots of rotary chunk k (16 rotate-half pairs) for this thread's row.
+  __device__ __forceinline__ void load_tab(int k, int64_t row, float4 (&t)[16]) const {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) t[j] = __ldg(tab + (int64_t)(16 * k + j) * tab_rows + row);
+  }
+
+  // One head row (128 accumulator columns) per call, in two passes so that the row
+  // never sits in registers whole: pass 1 sums the squares of the biased projection;
+  // pass 2 re-reads it, 16 rotate-half pairs at a time, normalises and rotates them.
+  // The RoPE tables come from a row-contiguous layout, so a warp's table load of its
+  // 32 consecutive rows is one 512-byte span, and the next chunk's tables are in flight
+  // while the current chunk is computed.
   template <class Put>
   __device__ __forceinline__ void fill(uint32_t tacc, int seg, int64_t row, int n0, Put put8) const {
-    float x[kHeadDim];
-#pragma unroll
-    for (int q4 = 0; q4 < kHeadDim / 32; ++q4) {
-      uint32_t v[32];
-      tmem_ld32(tacc + (uint32_t)(seg * kHeadDim + 32 * q4), v);
-      tmem_ld_wait();
-#pragma unroll
-      for (int j = 0; j < 32; ++j) x[32 * q4 + j] = __uint_as_float(v[j]);
-    }
     const int hd = heads * kHeadDim;
     const int col0 = n0 + seg * kHeadDim;
     const int part = col0 / hd;  // 0 q, 1 k, 2 v
-    if (bias != nullptr) {
+    const uint32_t t = tacc + (uint32_t)(seg * kHeadDim);
+    float r = 1.f;
+    const __nv_bfloat16* w = part == 0 ? wq : wk;
+    float4 cur[16];
+    if (part < 2) {
+      if constexpr (ROT > 0) load_tab(0, row, cur);
+      // pass 1: the sum of squares, in column order; the next 32 columns load meanwhile
+      float ss = 0.f;
+      uint32_t v[2][32];
+      tmem_ld32(t, v[0]);
+      tmem_ld_wait();
+      pin(v[0]);
 #pragma unroll
-      for (int c8 = 0; c8 < kHeadDim / 8; ++c8) {
-        const f8 bv = unpack8(ld_cached(bias + col0 + 8 * c8));
+      for (int q4 = 0; q4 < kHeadDim / 32; ++q4) {
+        if (q4 + 1 < kHeadDim / 32) tmem_ld32(t + (uint32_t)(32 * (q4 + 1)), v[(q4 + 1) & 1]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) x[8 * c8 + j] += bv.v[j];
+        for (int c8 = 0; c8 < 4; ++c8) {
+          float x[8];
+          biased8(v[q4 & 1] + 8 * c8, col0 + 32 * q4 + 8 * c8, x);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) ss += x[j] * x[j];
+        }
+        if (q4 + 1 < kHeadDim / 32) {
+          tmem_ld_wait();
+          pin(v[(q4 + 1) & 1]);
+        }
+      }
+      r = rsqrtf(ss / (float)kHeadDim + (part == 0 ? q_eps : k_eps));
+    }
+    if constexpr (ROT > 0) {
+      if (part < 2) {
+        // pass 2, rotary columns: pairs (c, c + kHalf) for c in [16k, 16k + 16)
+#pragma unroll
+        for (int k = 0; k < kHalf / 16; ++k) {
+          float4 nxt[16];
+          if (k + 1 < kHalf / 16) load_tab(k + 1, row, nxt);
+          uint32_t va[16], vb[16];
+          tmem_ld16(t + (uint32_t)(16 * k), va);
+          tmem_ld16(t + (uint32_t)(kHalf + 16 * k), vb);
+          tmem_ld_wait();
+          pin(va);
+          pin(vb);
+          const float* ca = reinterpret_cast<const float*>(cur);       // cos[c]
+          const float* sa = reinterpret_cast<const float*>(cur + 4);   // sin[c]
+          const float* cb = reinterpret_cast<const float*>(cur + 8);   // cos[c + kHalf]
+          const float* sb = reinterpret_cast<const float*>(cur + 12);  // sin[c + kHalf]
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            float a[8], b[8];
+            biased8(va + 8 * h, col0 + 16 * k + 8 * h, a);
+            biased8(vb + 8 * h, col0 + kHalf + 16 * k + 8 * h, b);
+            const f8 wa = unpack8(ld_cached(w + 16 * k + 8 * h));
+            const f8 wb = unpack8(ld_cached(w + kHalf + 16 * k + 8 * h));
+            float oa[8], ob[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+              const float an = a[j] * r * wa.v[j], bn = b[j] * r * wb.v[j];
+              const int c = 8 * h + j;
+              oa[j] = an * ca[c] + (-bn) * sa[c];  // first half takes -partner
+              ob[j] = bn * cb[c] + an * sb[c];
+            }
+            put8(2 * k + h, oa);
+            put8(kHalf / 8 + 2 * k + h, ob);
+          }
+          if (k + 1 < kHalf / 16) {
+#pragma unroll
+            for (int j = 0; j < 16; ++j) cur[j] = nxt[j];
+          }
+        }
       }
     }
     if (part < 2)
-      norm_rope_row<ROT>(x, part == 0 ? wq : wk, cos + row * ROT, sin + row * ROT,
-                         part == 0 ? q_eps : k_eps);
-#pragma unroll
-    for (int c8 = 0; c8 < kHeadDim / 8; ++c8) put8(c8, x + 8 * c8);
+      rest<ROT / 32>(t, col0, true, r, w, put8);
+    else
+      rest<0>(t, col0, false, 1.f, w, put8);
   }
+
+  // Columns [32 kFirst, 128) of the head row: normalised (q, k) or biased only (v),
+  // 32 at a time with the next 32 in flight.
+  template <int kFirst, class Put>
+  __device__ __forceinline__ void rest(uint32_t t, int col0, bool norm, float r,
+                                       const __nv_bfloat16* w, Put& put8) const {
+    if constexpr (kFirst < kHeadDim / 32) {
+      uint32_t v[2][32];
+      tmem_ld32(t + (uint32_t)(32 * kFirst), v[kFirst & 1]);
+      tmem_ld_wait();
+      pin(v[kFirst & 1]);
+#pragma unroll
+      for (int q4 = kFirst; q4 < kHeadDim / 32; ++q4) {
+        if (q4 + 1 < kHeadDim / 32) tmem_ld32(t + (uint32_t)(32 * (q4 + 1)), v[(q4 + 1) & 1]);
+#pragma unroll
+        for (int c8 = 0; c8 < 4; ++c8) {
+          const int c = 32 * q4 + 8 * c8;
+          float x[8];
+          biased8(v[q4 & 1] + 8 * c8, col0 + c, x);
+          if (norm) {
+            const f8 wv = unpack8(ld_cached(w + c));
+#pragma unroll
+            for (int j = 0; j < 8; ++j) x[j] = x[j] * r * wv.v[j];
+          }
+          put8(c / 8, x);
+        }
+        if (q4 + 1 < kHeadDim / 32) {
+          tmem_ld_wait();
+          pin(v[(q4 + 1) & 1]);
+        }
+      }
+    }
+  }
+
   __device__ __forceinline__ __nv_bfloat16* dest(int seg, int64_t row, int n0) const {
     const int hd = heads * kHeadDim;
     const int part = n0 / hd;
@@ -711,6 +807,25 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
   }
 }
 
+// The RoPE tables in the QKV epilogue's layout: float4 slot s of row r at
+// tab[s * rows + r], so that 32 consecutive rows of one slot are one 512-byte span.
+// Rotary chunk k (16 rotate-half pairs, half = rot / 2) owns slots 16k .. 16k + 15:
+// cos[16k, +16), sin[16k, +16), cos[half + 16k, +16), sin[half + 16k, +16).
+__global__ void rope_tables_kernel(float4* __restrict__ tab, const float* __restrict__ cos,
+                                   const float* __restrict__ sin, int64_t rows, int rot) {
+  const int half = rot / 2;
+  const int64_t n = rows * half;  // rot / 2 slots per row
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+       i += (int64_t)gridDim.x * blockDim.x) {
+    const int s = (int)(i / rows);
+    const int64_t r = i - (int64_t)s * rows;
+    const int k = s >> 4, j = s & 15;
+    const float* src = (j & 4) ? sin : cos;
+    const int col = ((j & 8) ? half : 0) + 16 * k + 4 * (j & 3);
+    tab[i] = __ldg(reinterpret_cast<const float4*>(src + r * rot + col));
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Host side
 // ---------------------------------------------------------------------------
@@ -838,16 +953,26 @@ int launch(const Common& c, const Epi& epi, const char* what, cudaStream_t strea
   return check_launch(what);
 }
 
-// QKV epilogue arguments and checks (both QKV entry points).
+// QKV epilogue arguments (both QKV entry points): the RoPE tables are relaid into
+// the workspace first, on the same stream.
 template <class Dst>
 int launch_qkv(const Common& c, const Dst& d, const void* bias, const void* q_weight,
-               const void* k_weight, const float* cos, const float* sin, int64_t heads,
-               int64_t rot, float q_eps, float k_eps, cudaStream_t stream) {
+               const void* k_weight, const float* cos, const float* sin, int64_t rows,
+               int64_t heads, int64_t rot, float q_eps, float k_eps, void* workspace,
+               cudaStream_t stream) {
+  auto* tab = static_cast<float4*>(workspace);
+  if (rot > 0) {
+    const int64_t n = rows * (rot / 2);
+    const int blocks = (int)std::min<int64_t>((n + 255) / 256, 148 * 8);
+    rope_tables_kernel<<<blocks, 256, 0, stream>>>(tab, cos, sin, rows, (int)rot);
+    const int rc = check_launch("h3b_qkv_gemm_pack");
+    if (rc != H3B_OK) return rc;
+  }
   auto go = [&](auto rot_tag) {
     constexpr int R = decltype(rot_tag)::value;
     QkvEpi<R, Dst> epi{static_cast<const __nv_bfloat16*>(bias),
                        static_cast<const __nv_bfloat16*>(q_weight),
-                       static_cast<const __nv_bfloat16*>(k_weight), cos, sin, q_eps, k_eps,
+                       static_cast<const __nv_bfloat16*>(k_weight), tab, rows, q_eps, k_eps,
                        (int)heads, d};
     return launch(c, epi, "h3b_qkv_gemm_pack", stream);
   };
@@ -857,6 +982,10 @@ int launch_qkv(const Common& c, const Dst& d, const void* bias, const void* q_we
     case 96: return go(std::integral_constant<int, 96>{});
     default: return go(std::integral_constant<int, 128>{});
   }
+}
+
+int64_t qkv_workspace_bytes(int64_t rows, int64_t rotary_dim) {
+  return rows * rotary_dim * 2 * (int64_t)sizeof(float);
 }
 
 // Shape checks of the QKV entry points (before the no-rows early return) ...
@@ -874,13 +1003,24 @@ int check_qkv_shape(int64_t heads, int64_t head_dim, int64_t rotary_dim) {
 
 // ... and their pointer checks (after it: empty tensors may carry null pointers).
 int check_qkv(const void* bias, const void* q_weight, const void* k_weight, const float* cos,
-              const float* sin, int64_t rotary_dim) {
+              const float* sin, int64_t rows, int64_t rotary_dim, const void* workspace,
+              int64_t workspace_bytes) {
   H3B_REQUIRE(q_weight != nullptr && k_weight != nullptr, "qkv_gemm_pack: null argument");
   H3B_REQUIRE(rotary_dim == 0 || (cos != nullptr && sin != nullptr),
               "qkv_gemm_pack: rotary tables missing");
   H3B_REQUIRE((bias == nullptr || aligned16(bias)) && aligned16(q_weight) && aligned16(k_weight) &&
                   (rotary_dim == 0 || (aligned16(cos) && aligned16(sin))),
               "qkv_gemm_pack: buffers must be 16-byte aligned");
+  const int64_t need = qkv_workspace_bytes(rows, rotary_dim);
+  if (need > 0 && (workspace == nullptr || workspace_bytes < need || !aligned16(workspace))) {
+    char buf[200];
+    snprintf(buf, sizeof(buf),
+             "h3b_qkv_gemm_pack: needs a 16-byte aligned workspace of %lld bytes for the RoPE "
+             "tables (got %lld)",
+             (long long)need, (long long)(workspace == nullptr ? 0 : workspace_bytes));
+    set_error(buf);
+    return H3B_ERR_VALUE;
+  }
   return H3B_OK;
 }
 
@@ -895,20 +1035,21 @@ extern "C" int h3b_qkv_gemm_pack(void* send, int64_t world, const void* x, int64
                                  const void* bias, const void* q_weight, const void* k_weight,
                                  const float* cos, const float* sin, int64_t heads,
                                  int64_t head_dim, int64_t rotary_dim, float q_eps, float k_eps,
-                                 h3b_stream_t stream) {
+                                 void* workspace, int64_t workspace_bytes, h3b_stream_t stream) {
   H3B_REQUIRE(world >= 1 && heads > 0 && heads % world == 0,
               "heads (%lld) must divide Ulysses degree (%lld)", (long long)heads, (long long)world);
   H3B_REQUIRE(rows >= 0 && dim > 0, "qkv_gemm_pack: bad shape");
   int rc = check_qkv_shape(heads, head_dim, rotary_dim);
   if (rc != H3B_OK || rows == 0) return rc;
-  if ((rc = check_qkv(bias, q_weight, k_weight, cos, sin, rotary_dim)) != H3B_OK) return rc;
+  rc = check_qkv(bias, q_weight, k_weight, cos, sin, rows, rotary_dim, workspace, workspace_bytes);
+  if (rc != H3B_OK) return rc;
   Common c;
   rc = prepare(c, "h3b_qkv_gemm_pack", x, rows, dim, x_row_stride, w_qkv, 3 * heads * kHeadDim);
   if (rc != H3B_OK) return rc;
   H3B_REQUIRE(send != nullptr && aligned16(send), "qkv_gemm_pack: send must be 16-byte aligned");
   LocalSend d{static_cast<__nv_bfloat16*>(send), rows, (int)(heads / world)};
-  return launch_qkv(c, d, bias, q_weight, k_weight, cos, sin, heads, rotary_dim, q_eps, k_eps,
-                    static_cast<cudaStream_t>(stream));
+  return launch_qkv(c, d, bias, q_weight, k_weight, cos, sin, rows, heads, rotary_dim, q_eps,
+                    k_eps, workspace, static_cast<cudaStream_t>(stream));
 }
 
 extern "C" int h3b_qkv_gemm_pack_p2p(void* const* recv_ptrs, int64_t world, int64_t row_offset,
@@ -917,7 +1058,8 @@ extern "C" int h3b_qkv_gemm_pack_p2p(void* const* recv_ptrs, int64_t world, int6
                                      const void* bias, const void* q_weight,
                                      const void* k_weight, const float* cos, const float* sin,
                                      int64_t heads, int64_t head_dim, int64_t rotary_dim,
-                                     float q_eps, float k_eps, h3b_stream_t stream) {
+                                     float q_eps, float k_eps, void* workspace,
+                                     int64_t workspace_bytes, h3b_stream_t stream) {
   H3B_REQUIRE(world >= 1 && world <= kMaxPeers && heads > 0 && heads % world == 0,
               "heads (%lld) must divide Ulysses degree (%lld), world <= %d", (long long)heads,
               (long long)world, kMaxPeers);
@@ -928,7 +1070,8 @@ extern "C" int h3b_qkv_gemm_pack_p2p(void* const* recv_ptrs, int64_t world, int6
   H3B_REQUIRE(dim > 0, "qkv_gemm_pack: bad shape");
   int rc = check_qkv_shape(heads, head_dim, rotary_dim);
   if (rc != H3B_OK || rows == 0) return rc;
-  if ((rc = check_qkv(bias, q_weight, k_weight, cos, sin, rotary_dim)) != H3B_OK) return rc;
+  rc = check_qkv(bias, q_weight, k_weight, cos, sin, rows, rotary_dim, workspace, workspace_bytes);
+  if (rc != H3B_OK) return rc;
   Common c;
   rc = prepare(c, "h3b_qkv_gemm_pack_p2p", x, rows, dim, x_row_stride, w_qkv,
                3 * heads * kHeadDim);
@@ -942,8 +1085,16 @@ extern "C" int h3b_qkv_gemm_pack_p2p(void* const* recv_ptrs, int64_t world, int6
   }
   d.row_offset = row_offset;
   d.hl = (int)(heads / world);
-  return launch_qkv(c, d, bias, q_weight, k_weight, cos, sin, heads, rotary_dim, q_eps, k_eps,
-                    static_cast<cudaStream_t>(stream));
+  return launch_qkv(c, d, bias, q_weight, k_weight, cos, sin, rows, heads, rotary_dim, q_eps,
+                    k_eps, workspace, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int h3b_qkv_gemm_pack_workspace_size(int64_t rows, int64_t rotary_dim,
+                                                int64_t* bytes_out) {
+  H3B_REQUIRE(bytes_out != nullptr, "qkv_gemm_pack_workspace_size: null output pointer");
+  H3B_REQUIRE(rows >= 0 && rotary_dim >= 0, "qkv_gemm_pack_workspace_size: negative shape");
+  *bytes_out = qkv_workspace_bytes(rows, rotary_dim);
+  return H3B_OK;
 }
 
 extern "C" int h3b_gemm(void* out, int64_t out_row_stride, const void* x, int64_t rows,

@@ -244,7 +244,9 @@ def qkv_gemm_pack_supported(x: torch.Tensor, weight: torch.Tensor, heads: int, h
 
 
 def qkv_gemm_pack_args(op, x, weight, bias, q_weight, k_weight, cos, sin, heads):
-    """Checks shared by the GEMM packing ops; returns (x2d, weight, bias, rotary_dim, cos32, sin32)."""
+    """Checks shared by the GEMM packing ops; returns (x2d, weight, bias, rotary_dim, cos32,
+    sin32, workspace): the workspace is the scratch the kernel relays the RoPE tables into
+    (rows * rotary_dim * 8 bytes, None without RoPE)."""
 
     require_cuda(op, x, weight, q_weight, k_weight)
     require_bf16(op, x, weight, q_weight, k_weight)
@@ -256,13 +258,14 @@ def qkv_gemm_pack_args(op, x, weight, bias, q_weight, k_weight, cos, sin, heads)
         require_bf16(op, bias)
         bias = bias.contiguous()
     if cos is None:
-        return x2d, weight, bias, 0, None, None
+        return x2d, weight, bias, 0, None, None, None
     rotary_dim = cos.shape[-1]
     cos32 = cos.to(torch.float32).contiguous()
     sin32 = sin.to(torch.float32).contiguous()
     if cos32.shape[0] != x2d.shape[0]:
         raise ValueError(f"{op}: rotary tables have {cos32.shape[0]} rows, x has {x2d.shape[0]}")
-    return x2d, weight, bias, rotary_dim, cos32, sin32
+    workspace = torch.empty(2 * cos32.numel(), dtype=torch.float32, device=cos32.device)
+    return x2d, weight, bias, rotary_dim, cos32, sin32, workspace
 
 
 def fused_qkv_gemm_pack(x, weight, bias, q_weight, k_weight, cos, sin, heads, world, q_eps, k_eps,
@@ -276,8 +279,8 @@ def fused_qkv_gemm_pack(x, weight, bias, q_weight, k_weight, cos, sin, heads, wo
     op = "fused_qkv_gemm_pack"
     if heads % world:
         raise ValueError(f"heads ({heads}) must divide Ulysses degree ({world})")
-    x2d, weight, bias, rotary_dim, cos32, sin32 = qkv_gemm_pack_args(op, x, weight, bias, q_weight,
-                                                                    k_weight, cos, sin, heads)
+    x2d, weight, bias, rotary_dim, cos32, sin32, workspace = qkv_gemm_pack_args(
+        op, x, weight, bias, q_weight, k_weight, cos, sin, heads)
     rows, dim = x2d.shape
     if out is None:
         out = torch.empty((world, rows, heads // world, 3 * 128), dtype=x.dtype, device=x.device)
@@ -287,7 +290,8 @@ def fused_qkv_gemm_pack(x, weight, bias, q_weight, k_weight, cos, sin, heads, wo
          ptr(bias) if bias is not None else None, ptr(q_weight.contiguous()),
          ptr(k_weight.contiguous()), ptr(cos32) if cos32 is not None else None,
          ptr(sin32) if sin32 is not None else None, heads, 128, rotary_dim, float(q_eps),
-         float(k_eps), stream_of(x))
+         float(k_eps), ptr(workspace) if workspace is not None else None,
+         workspace.numel() * 4 if workspace is not None else 0, stream_of(x))
     return out
 
 

@@ -180,7 +180,7 @@ class PeerExchange:
         except that the projection is not rounded to bf16 before the norm)."""
 
         op = "fused_qkv_gemm_pack_p2p"
-        x2d, weight, bias, rotary_dim, cos32, sin32 = qkv_gemm_pack_args(
+        x2d, weight, bias, rotary_dim, cos32, sin32, workspace = qkv_gemm_pack_args(
             op, x, weight, bias, q_weight, k_weight, cos, sin, heads)
         rows, dim = x2d.shape
         if rows != counts[self.rank]:
@@ -193,7 +193,9 @@ class PeerExchange:
              ptr(x2d), rows, dim, x2d.stride(0), ptr(weight), ptr(bias) if bias is not None else None,
              ptr(q_weight.contiguous()), ptr(k_weight.contiguous()),
              ptr(cos32) if cos32 is not None else None, ptr(sin32) if sin32 is not None else None,
-             heads, 128, rotary_dim, float(q_eps), float(k_eps), stream_of(x2d))
+             heads, 128, rotary_dim, float(q_eps), float(k_eps),
+             ptr(workspace) if workspace is not None else None,
+             workspace.numel() * 4 if workspace is not None else 0, stream_of(x2d))
 
     def check(self) -> None:
         """Raise if a barrier of an earlier call gave up on a peer (status bit 2,

@@ -30,7 +30,7 @@ typedef struct CUstream_st* h3b_stream_t; /* == cudaStream_t */
 #define H3B_ERR_CUDA 2        /* CUDA launch or driver error: RuntimeError         */
 #define H3B_ERR_UNSUPPORTED 3 /* valid input this build does not handle: RuntimeError */
 
-#define H3B_ABI_VERSION 7
+#define H3B_ABI_VERSION 8
 
 int h3b_abi_version(void);
 /* Kernels launched through this library by this process (all devices and host
@@ -140,14 +140,23 @@ int h3b_qknorm_rope_pack(void* send, const void* q, const void* k, const void* v
  * h3b_qknorm_rope_pack lays them out (send [world, rows, hl, 3*head_dim]). The
  * projection is not rounded to bf16 before the norm (one rounding, at the store).
  * Needs head_dim 128, an even head count, dim % 64 == 0 and rotary_dim in
- * {0, 64, 96, 128} (else H3B_ERR_UNSUPPORTED).
+ * {0, 64, 96, 128} (else H3B_ERR_UNSUPPORTED). With rotary_dim > 0 the call first
+ * relays the RoPE tables into `workspace` (16-byte aligned, at least the bytes
+ * h3b_qkv_gemm_pack_workspace_size reports: rows * rotary_dim * 8, caller-owned,
+ * only used during the call's kernels) so that the epilogue reads them row-
+ * contiguously; a null or short workspace is H3B_ERR_VALUE.
  * replaces to_q/to_k/to_v + fused_qknorm_rope (x2) + pack_qkv_destination_major
  *          packed_ulysses.py:166-200, relayout.py:97-130 */
 int h3b_qkv_gemm_pack(void* send, int64_t world, const void* x, int64_t rows, int64_t dim,
                       int64_t x_row_stride, const void* w_qkv, const void* bias,
                       const void* q_weight, const void* k_weight, const float* cos,
                       const float* sin, int64_t heads, int64_t head_dim, int64_t rotary_dim,
-                      float q_eps, float k_eps, h3b_stream_t stream);
+                      float q_eps, float k_eps, void* workspace, int64_t workspace_bytes,
+                      h3b_stream_t stream);
+
+/* Bytes of workspace h3b_qkv_gemm_pack and h3b_qkv_gemm_pack_p2p need for `rows`
+ * local rows (0 without RoPE). Host-only; launches nothing. */
+int h3b_qkv_gemm_pack_workspace_size(int64_t rows, int64_t rotary_dim, int64_t* bytes_out);
 
 /* out[row, :n] = act(x W^T + bias): x [rows, dim] (row stride x_row_stride),
  * W [n, dim] row-major (nn.Linear layout), bias [n] or NULL, out row stride
@@ -290,7 +299,8 @@ int h3b_qknorm_rope_pack_p2p(void* const* recv_ptrs, int64_t world, int64_t row_
 /* h3b_qkv_gemm_pack with the epilogue storing each head row straight into its
  * owner's receive buffer, at the layout of h3b_qknorm_rope_pack_p2p: the QKV
  * exchange runs inside the GEMM, overlapped with the tiles still computing.
- * Same bits as h3b_qkv_gemm_pack followed by an exchange of its send buffer.
+ * Same bits as h3b_qkv_gemm_pack followed by an exchange of its send buffer;
+ * workspace as for h3b_qkv_gemm_pack.
  * replaces the QKV projection, the pack and the QKV exchange of
  *          packed_ulysses.py:166-200, :85-108 */
 int h3b_qkv_gemm_pack_p2p(void* const* recv_ptrs, int64_t world, int64_t row_offset,
@@ -298,7 +308,8 @@ int h3b_qkv_gemm_pack_p2p(void* const* recv_ptrs, int64_t world, int64_t row_off
                           int64_t x_row_stride, const void* w_qkv, const void* bias,
                           const void* q_weight, const void* k_weight, const float* cos,
                           const float* sin, int64_t heads, int64_t head_dim,
-                          int64_t rotary_dim, float q_eps, float k_eps, h3b_stream_t stream);
+                          int64_t rotary_dim, float q_eps, float k_eps, void* workspace,
+                          int64_t workspace_bytes, h3b_stream_t stream);
 
 /* out is this rank's attention output [S_total, heads_local, head_dim]
  * (contiguous); global row s, owned by rank o (row_counts[] gives every rank's

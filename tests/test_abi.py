@@ -102,7 +102,8 @@ def test_qkv_gemm_pack_argument_errors_without_a_gpu():
 
     def call(heads, head_dim, rot, world=1, dim=256):
         _lib.call("h3b_qkv_gemm_pack", fake, world, args["x"], args["rows"], dim, dim, args["w"], None,
-                  args["wq"], args["wk"], args["cos"], args["sin"], heads, head_dim, rot, 1e-6, 1e-6, None)
+                  args["wq"], args["wk"], args["cos"], args["sin"], heads, head_dim, rot, 1e-6, 1e-6, fake,
+                  args["rows"] * rot * 8, None)
 
     with pytest.raises(ValueError, match="must divide Ulysses degree"):
         call(heads=4, head_dim=128, rot=96, world=3)
@@ -114,6 +115,12 @@ def test_qkv_gemm_pack_argument_errors_without_a_gpu():
         call(heads=4, head_dim=128, rot=48)
     with pytest.raises(RuntimeError, match="dim % 64"):
         call(heads=4, head_dim=128, rot=96, dim=200)
+    with pytest.raises(ValueError, match="workspace of 49152 bytes"):
+        _lib.call("h3b_qkv_gemm_pack", fake, 1, fake, 64, 256, 256, fake, None, fake, fake, fake, fake, 4, 128, 96,
+                  1e-6, 1e-6, fake, 64 * 96 * 8 - 16, None)
+    need = ctypes.c_int64(-1)
+    _lib.call("h3b_qkv_gemm_pack_workspace_size", 64, 96, ctypes.byref(need))
+    assert need.value == 64 * 96 * 8
 
 
 def test_qkv_gemm_pack_without_rows_is_a_noop_without_a_gpu():
@@ -121,9 +128,9 @@ def test_qkv_gemm_pack_without_rows_is_a_noop_without_a_gpu():
 
     _lib.reset_launch_count()
     _lib.call("h3b_qkv_gemm_pack", None, 1, None, 0, 256, 256, None, None, None, None, None, None,
-              2, 128, 96, 1e-6, 1e-6, None)
+              2, 128, 96, 1e-6, 1e-6, None, 0, None)
     _lib.call("h3b_qkv_gemm_pack_p2p", (ctypes.c_void_p * 1)(1 << 20), 1, 0, 0, None, 0, 256, 256, None, None,
-              None, None, None, None, 2, 128, 96, 1e-6, 1e-6, None)
+              None, None, None, None, 2, 128, 96, 1e-6, 1e-6, None, 0, None)
     assert _lib.launch_count() == 0
 
 

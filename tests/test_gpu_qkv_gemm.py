@@ -95,9 +95,10 @@ def test_qkv_gemm_pack_p2p_routes_rows_to_owners(rows, dim, heads, world, offset
     hl = heads // world
     recv = [torch.full((total, hl, 384), float("nan"), device="cuda").to(torch.bfloat16) for _ in range(world)]
     ptrs = (ctypes.c_void_p * world)(*[t.data_ptr() for t in recv])
+    ws = torch.empty(rows * 96 * 2, dtype=torch.float32, device="cuda")
     _lib.call("h3b_qkv_gemm_pack_p2p", ptrs, world, offset, total, x.data_ptr(), rows, dim, dim, w.data_ptr(),
               b.data_ptr(), wq.data_ptr(), wk.data_ptr(), cos.data_ptr(), sin.data_ptr(), heads, 128, 96,
-              1e-6, 1e-6, torch.cuda.current_stream().cuda_stream)
+              1e-6, 1e-6, ws.data_ptr(), ws.numel() * 4, torch.cuda.current_stream().cuda_stream)
     local = torch.empty((world, rows, hl, 384), device="cuda").to(torch.bfloat16)
     from h3_flash_b200.runtime.kernels.fusions import fused_qkv_gemm_pack
 
