@@ -504,7 +504,10 @@ enum Activation : int { kActNone = 0, kActGeluTanh = 1 };
 template <int ACT>
 struct DenseEpi {
   static constexpr int kSegments = 2;
-  static constexpr bool kStaged = false;
+  // Whole-row stores through the staging buffer: measured 0.69-0.80 against 0.82 ms
+  // for the direct row-piece stores on the attention output projection, and no slower
+  // on the FFN projection; the QKV and gated-residual epilogues measured faster direct.
+  static constexpr bool kStaged = true;
   __nv_bfloat16* out;
   int64_t ldo;
   const __nv_bfloat16* bias;  // [N] or nullptr
