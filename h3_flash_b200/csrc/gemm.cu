@@ -184,6 +184,30 @@ __device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap
       : "memory");
 }
 
+// 2-D TMA store of a shared-memory box to global memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, uint32_t src, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(src), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// This thread's bulk stores have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// This thread's bulk stores are complete.
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Generic-proxy shared-memory writes become visible to the async proxy (TMA).
+__device__ __forceinline__ void fence_async_shared() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 __device__ __forceinline__ void prefetch_map(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -341,6 +365,7 @@ template <int ROT, class Dst>
 struct QkvEpi {
   static constexpr int kSegments = 2;
   static constexpr bool kStaged = Dst::kStaged;
+  static constexpr bool kTmaStore = false;
   static constexpr int kHalf = ROT / 2;
   static_assert(kHalf % 16 == 0, "rotary width: a multiple of 32");
   const __nv_bfloat16* bias;  // [3 H D] or nullptr
@@ -504,10 +529,12 @@ enum Activation : int { kActNone = 0, kActGeluTanh = 1 };
 template <int ACT>
 struct DenseEpi {
   static constexpr int kSegments = 2;
-  // Whole-row stores through the staging buffer: measured 0.69-0.80 against 0.82 ms
-  // for the direct row-piece stores on the attention output projection, and no slower
-  // on the FFN projection; the QKV and gated-residual epilogues measured faster direct.
+  // The segment goes through the staging buffer and leaves as two TMA stores (see the
+  // epilogue role); the QKV and gated-residual epilogues measured faster storing each
+  // thread's row directly.
   static constexpr bool kStaged = true;
+  static constexpr bool kTmaStore = true;
+  CUtensorMap out_map;  // out [rows, N], (64, 32) box, 128-byte swizzle
   __nv_bfloat16* out;
   int64_t ldo;
   const __nv_bfloat16* bias;  // [N] or nullptr
@@ -547,6 +574,7 @@ struct DenseEpi {
 struct GatedResidualEpi {
   static constexpr int kSegments = 2;
   static constexpr bool kStaged = false;
+  static constexpr bool kTmaStore = false;
   __nv_bfloat16* out;
   int64_t ldo;
   const __nv_bfloat16* bias;      // [N] or nullptr
@@ -594,6 +622,7 @@ struct GatedResidualEpi {
 struct SwigluEpi {
   static constexpr int kSegments = 1;
   static constexpr bool kStaged = false;
+  static constexpr bool kTmaStore = false;
   __nv_bfloat16* out;
   int64_t ldo;
   const __nv_bfloat16* bias;  // interleaved like W, [2 n] or nullptr
@@ -635,7 +664,8 @@ struct SwigluEpi {
 template <class Epi>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap x_map,
-                const __grid_constant__ CUtensorMap w_map, const Shape prm, const Epi epi) {
+                const __grid_constant__ CUtensorMap w_map, const Shape prm,
+                const __grid_constant__ Epi epi) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -741,11 +771,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const uint32_t lane_base = (uint32_t)(quad * 32) << 16;
     uint8_t* stage = smem + kSmemEpi + (warp - 2) * kEpiStageBytes;
-    // Chunk c (16 bytes) of staging row r sits at position c ^ (r & 15).
+    // Staging layouts. Plain stores: chunk c (16 bytes) of staging row r sits at
+    // position c ^ (r & 15) of the row's 256 bytes. TMA stores: two 64-column boxes of
+    // 32 rows x 128 bytes in the 128-byte swizzle (chunk c % 8 of row r at position
+    // (c % 8) ^ (r % 8)), one per half of the segment. Both keep the per-thread row
+    // writes and the per-warp reads free of bank conflicts.
     uint8_t* my_row = stage + lane * kSegBytes;
     __nv_bfloat16* direct = nullptr;  // unstaged epilogues: this thread's row segment
     auto put8 = [&](int c, const float* v) {
-      if constexpr (Epi::kStaged)
+      if constexpr (Epi::kTmaStore)
+        *reinterpret_cast<uint4*>(stage + (c >> 3) * (kEpiStageBytes / 2) + lane * 128 +
+                                  (((c & 7) ^ (lane & 7)) << 4)) = pack8(v);
+      else if constexpr (Epi::kStaged)
         *reinterpret_cast<uint4*>(my_row + ((c ^ (lane & 15)) << 4)) = pack8(v);
       else if (direct != nullptr)
         *reinterpret_cast<uint4*>(direct + 8 * c) = pack8(v);
@@ -769,7 +806,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // Rows past the end compute on the accumulator's padding rows (TMA filled
         // their x with zeros) and are never stored.
         if constexpr (!Epi::kStaged) direct = my < prm.rows ? epi.dest(seg, my, n0) : nullptr;
+        if constexpr (Epi::kTmaStore) {
+          // The previous segment's stores have read the staging buffer.
+          if (lane == 0) bulk_wait_read();
+          __syncwarp();
+        }
         epi.fill(tacc, seg, my < prm.rows ? my : prm.rows - 1, n0, put8);
+        if constexpr (Epi::kTmaStore) {
+          // Rows past the end lie outside the tensor map: the TMA unit drops them.
+          fence_async_shared();
+          __syncwarp();
+          if (lane == 0) {
+            const int col = n0 + seg * kHeadDim;
+            tma_store_2d(&epi.out_map, smem_u32(stage), col, (int)row0);
+            tma_store_2d(&epi.out_map, smem_u32(stage + kEpiStageBytes / 2), col + 64, (int)row0);
+            bulk_commit();
+          }
+          continue;
+        }
         if constexpr (!Epi::kStaged) continue;
         __syncwarp();
         // Two whole rows per instruction: lanes 0-15 row i, lanes 16-31 row i + 1.
@@ -789,6 +843,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(map_to_cta(bar_tempty(b), 0));
+    }
+    if constexpr (Epi::kTmaStore) {
+      if (lane == 0) bulk_wait_all();
     }
     epi.finish();
   }
@@ -866,6 +923,30 @@ int make_map(CUtensorMap* map, const void* base, int64_t k, int64_t rows, int64_
     char buf[256];
     snprintf(buf, sizeof(buf), "h3b_gemm: tensor map for %s rejected (CUresult %d)",
              name, (int)r);
+    set_error(buf);
+    return H3B_ERR_CUDA;
+  }
+  return H3B_OK;
+}
+
+// 2-D map over (N, rows) of the bf16 output, row stride ldo, with the epilogue's
+// (64, 32) store box in the 128-byte swizzle.
+int make_out_map(CUtensorMap* map, void* out, int64_t n, int64_t rows, int64_t ldo) {
+  auto fn = encode_fn();
+  if (fn == nullptr) {
+    set_error("h3b_gemm: cuTensorMapEncodeTiled is unavailable");
+    return H3B_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)n, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ldo * 2};
+  cuuint32_t box[2] = {64, 32};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, out, dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    char buf[256];
+    snprintf(buf, sizeof(buf), "h3b_gemm: tensor map for out rejected (CUresult %d)", (int)r);
     set_error(buf);
     return H3B_ERR_CUDA;
   }
@@ -1114,8 +1195,11 @@ extern "C" int h3b_gemm(void* out, int64_t out_row_stride, const void* x, int64_
   auto* o = static_cast<__nv_bfloat16*>(out);
   auto* b = static_cast<const __nv_bfloat16*>(bias);
   const auto s = static_cast<cudaStream_t>(stream);
-  if (activation == kActGeluTanh) return launch(c, DenseEpi<kActGeluTanh>{o, out_row_stride, b}, "h3b_gemm", s);
-  return launch(c, DenseEpi<kActNone>{o, out_row_stride, b}, "h3b_gemm", s);
+  CUtensorMap om;
+  if ((rc = make_out_map(&om, out, n, rows, out_row_stride)) != H3B_OK) return rc;
+  if (activation == kActGeluTanh)
+    return launch(c, DenseEpi<kActGeluTanh>{om, o, out_row_stride, b}, "h3b_gemm", s);
+  return launch(c, DenseEpi<kActNone>{om, o, out_row_stride, b}, "h3b_gemm", s);
 }
 
 extern "C" int h3b_gemm_swiglu(void* out, int64_t out_row_stride, const void* x, int64_t rows,
