@@ -1099,6 +1099,24 @@ def profile_kernel(args) -> None:
         out = torch.empty((world, rows, args.heads_per_rank, 3 * cfg.head_dim), device="cuda", dtype=torch.bfloat16)
         for _ in range(args.warmup + args.steps):
             fused_qkv_gemm_pack(x, w, b, norm, norm, cos, sin, cfg.heads, world, cfg.eps, cfg.eps, out=out)
+    elif args.profile_kernel == "gemm_gated":
+        # The FFN output projection with the closing gated residual in the epilogue,
+        # one rank's rows at the SP layout given by --heads-per-rank (24: the N=1 shape):
+        # x [rows, 12288], W [3072, 12288], residual and output [rows, 3072].
+        from h3_flash_b200.runtime.kernels.fusions import fused_linear_gated_residual
+
+        world = cfg.heads // args.heads_per_rank
+        rows = cfg.seq // world
+        g = torch.Generator(device="cuda").manual_seed(0)
+        x = torch.randn(rows, cfg.ffn_inner, device="cuda", generator=g).to(torch.bfloat16)
+        w = (0.02 * torch.randn(cfg.dim, cfg.ffn_inner, device="cuda", generator=g)).to(torch.bfloat16)
+        b = (0.02 * torch.randn(cfg.dim, device="cuda", generator=g)).to(torch.bfloat16)
+        res = torch.randn(rows, cfg.dim, device="cuda", generator=g).to(torch.bfloat16)
+        gate = (0.1 * torch.randn(3, cfg.dim, device="cuda", generator=g)).to(torch.bfloat16)
+        idx = torch.arange(rows, device="cuda") % 3
+        out = torch.empty((rows, cfg.dim), device="cuda", dtype=torch.bfloat16)
+        for _ in range(args.warmup + args.steps):
+            fused_linear_gated_residual(x, w, b, res, gate, idx, out=out)
     elif args.profile_kernel == "gemm_gelu":
         # The FFN projection with GELU-tanh in the GEMM epilogue, one rank's rows at
         # the SP layout given by --heads-per-rank (24: the N=1 shape).
@@ -1342,7 +1360,8 @@ def main() -> int:
     parser.add_argument("--no-eager-baseline", action="store_true",
                         help="skip timing the unfused torch block at N=1")
     parser.add_argument("--sweep", choices=["elementwise"], help="print the config-2 kernel sweep instead")
-    parser.add_argument("--profile-kernel", choices=["attention", "elementwise", "qkv_gemm", "gemm_gelu"],
+    parser.add_argument("--profile-kernel", choices=["attention", "elementwise", "qkv_gemm", "gemm_gelu",
+                                                     "gemm_gated"],
                         help="launch one kernel family for an ncu capture")
     parser.add_argument("--heads-per-rank", type=int, default=3)
     parser.add_argument("--exchange-bench", action="store_true",
