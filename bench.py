@@ -18,11 +18,11 @@ D2H back to back for each step. For N>1 each rank first binds to the CPU cores t
 reports as local to its GPU, so that its pinned buffers sit on that NUMA node.
 ``roofline`` covers the dominant kernel (attention) from CUDA events
 around its launches inside the timed steps. ``cpu_baseline`` times the CPU oracle
-port of the reference path (two gloo ranks) on the BASELINE CPU configuration.
+port of the reference path (two gloo ranks) on the benchmark CPU configuration.
 
 ``--impl reference`` times that CPU port as the reference arm (rank 0 only).
 
-Other modes print their own line: ``--sweep elementwise``,
+Other modes print their own line: ``--sweep elementwise`` (benchmark config 2),
 ``--exchange-bench`` (N>1: the exchange operations alone), ``--transformer-bench``
 (the whole H3 transformer per request: invariant caches at N=1, rank-local I/O at N>1),
 ``--profile-kernel`` (one kernel for ncu captures).
@@ -922,7 +922,7 @@ def gemm_ab(cfg, steps: int, flush) -> dict:
 
 
 def side_block(stack, config: str, steps: int, flush) -> dict:
-    """The installed (fused) block stack at another BASELINE shape on one GPU: ms per
+    """The installed (fused) block stack at another benchmark shape on one GPU: ms per
     block forward and the in-step attention rate. Inputs seeded like the main line."""
 
     from h3_flash_b200.runtime.timing import TIMER
@@ -951,7 +951,7 @@ def side_block(stack, config: str, steps: int, flush) -> dict:
 
 
 def sp_side_block(stack, runtime, config: str, rank: int, world: int, steps: int, flush) -> dict:
-    """The installed packed-Ulysses block stack at another BASELINE shape over the same
+    """The installed packed-Ulysses block stack at another benchmark shape over the same
     ranks (every rank calls it; a new request, so the row counts are exchanged again):
     ms per block forward (max over ranks) and the in-step attention rate."""
 
@@ -1014,7 +1014,7 @@ def _timed(fn, steps: int, warmup: int, flush: torch.Tensor) -> float:
 
 
 def elementwise_sweep(args) -> dict:
-    """BASELINE config 2: each fused elementwise kernel at the 1xB200 sweep shapes;
+    """Benchmark config 2: each fused elementwise kernel at the 1xB200 sweep shapes;
     achieved GB/s = algorithmic bytes (each input read once, each output written once)
     / CUDA-event time, L2 flushed between launches."""
 
@@ -1028,7 +1028,7 @@ def elementwise_sweep(args) -> dict:
     rnd = lambda *shape, std=1.0, mean=0.0: (torch.randn(*shape, device="cuda", generator=g) * std + mean).to(  # noqa: E731
         torch.bfloat16)
     x, br = rnd(1, s, d), rnd(1, s, d)
-    scale_v, shift_v, gate_v = rnd(d, std=0.1), rnd(d, std=0.1), rnd(d, std=0.1)  # BASELINE [d] vectors
+    scale_v, shift_v, gate_v = rnd(d, std=0.1), rnd(d, std=0.1), rnd(d, std=0.1)  # benchmark [d] vectors
     table = rnd(3, 6 * d, std=0.1)
     t = table.chunk(6, -1)
     idx = torch.ones(s, dtype=torch.long, device="cuda")

@@ -6,7 +6,7 @@ are fresh tensors, inputs are never mutated, non-contiguous activations are
 copied). The reference's Triton kernels become calls into libh3b.so; there is
 no CPU path, non-CUDA tensors raise.
 
-Additional ops the BASELINE block needs (no reference kernel): ``fused_modulate``,
+Additional ops the benchmark block needs (no reference kernel): ``fused_modulate``,
 ``fused_gated_residual``, ``fused_gelu_tanh`` and ``fused_qknorm_rope_pack``
 (QK-norm + RoPE fused with the packed-Ulysses destination-major pack).
 """
@@ -132,7 +132,7 @@ def fused_qknorm_rope(x, weight, cos, sin, eps):
 
 
 def fused_modulate(x, scale, shift, index=None):
-    """AdaLN modulate without the norm: x*(1+scale[idx])+shift[idx] (BASELINE op).
+    """AdaLN modulate without the norm: x*(1+scale[idx])+shift[idx] (benchmark op).
     scale/shift are [d] vectors or [n_table, d] tables addressed through ``index``."""
 
     op = "fused_modulate"

@@ -11,7 +11,7 @@ Block math (kernels/transformer.py:50-126):
   normed  = RMSNorm(h)*(1+scale_msa[idx]) + shift_msa[idx]            (fused_rmsnorm_modulate)
   a       = attn(normed, rotary_emb)
   h, normed = h + gate_msa[idx]*a, RMSNorm(h)*(1+scale_mlp)+shift_mlp  (fused_residual_gate_rmsnorm_modulate)
-  f       = ff(normed)          # SwiGLU (H3) or GELU-tanh (BASELINE) activation fused
+  f       = ff(normed)          # SwiGLU (H3) or GELU-tanh (benchmark) activation fused
   return h + gate_mlp[idx]*f                                           (fused_gated_residual)
 """
 
@@ -237,7 +237,7 @@ def install_transformer_fusions(transformer: Any, *, modulate: bool = True, swig
                                 qknorm_rope: bool = True, gemm_epilogue: bool = True,
                                 gemm_pack: bool = True) -> dict[str, Any]:
     """kernels/transformer.py:207-228. ``swiglu`` toggles the fused FFN activation
-    (SwiGLU for H3, GELU-tanh for the BASELINE block). ``gemm_epilogue`` runs the
+    (SwiGLU for H3, GELU-tanh for the benchmark block). ``gemm_epilogue`` runs the
     activation inside the FFN projection GEMM (the h3b tcgen05 GEMM's epilogue; SwiGLU
     on a weight whose value and gate rows are interleaved once and cached) instead of
     the h3b elementwise kernel after a cuBLAS GEMM.

@@ -1,7 +1,7 @@
-"""BASELINE workload shapes and seeded synthetic inputs for the LOSSLESS DiT block.
+"""Benchmark workload shapes and seeded synthetic inputs for the LOSSLESS DiT block.
 
 Shapes (d=3072, 24 heads x 128, FFN 4x GELU-tanh) and token counts are the
-BASELINE configurations; weights are random-init N(0, 0.02), activations
+benchmark configurations; weights are random-init N(0, 0.02), activations
 N(0, 1), AdaLN shift/scale/gate tables N(0, 0.1), RMSNorm/QK-norm weights
 N(1, 0.02). RoPE tables follow the H3 structure (rank_local_io.py:74-80): per-axis
 angles pos_axis * inv_freq_axis for (t, h, w), concatenated, then duplicated

@@ -101,7 +101,7 @@ int h3b_swiglu(void* out, const void* x, int64_t rows, int64_t n,
                int64_t in_row_stride, int64_t out_row_stride, h3b_stream_t stream);
 
 /* out = gelu(x, approximate="tanh") elementwise over rows x cols
- * the FFN activation of the BASELINE block (torch.nn.functional.gelu semantics) */
+ * the FFN activation of the benchmark block (torch.nn.functional.gelu semantics) */
 int h3b_gelu_tanh(void* out, const void* x, int64_t rows, int64_t cols,
                   int64_t in_row_stride, int64_t out_row_stride, h3b_stream_t stream);
 

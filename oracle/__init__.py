@@ -6,7 +6,7 @@ can be checked against it:
 
 * ``bf16``           — bfloat16 bit helpers (round-to-nearest-even, ulp distance).
 * ``fusions_ref``    — the reference Triton fusions (src/h3_flash/runtime/kernels/fusions.py)
-                       and the BASELINE eager ops, in numpy fp32/fp64.
+                       and the benchmark eager ops, in numpy fp32/fp64.
 * ``relayout_ref``   — pack / merge relayouts (src/h3_flash/runtime/parallel/relayout.py).
 * ``attention_ref``  — dense softmax attention in fp32/fp64 (the SDPA call at
                        src/h3_flash/runtime/parallel/packed_ulysses.py:201-209).

@@ -14,7 +14,7 @@ unfused branches) with the packed-Ulysses attention
   h      = h + gate_mlp[idx] * (act(normed W_1^T + b_1) W_2^T + b_2)    act = GELU-tanh | SwiGLU
 
 Used as the fp32 reference of the block-level parity tests and as the timed
-CPU baseline (BASELINE config "CPU/gloo world_size=2").
+CPU baseline (benchmark config "CPU/gloo world_size=2").
 """
 
 from __future__ import annotations

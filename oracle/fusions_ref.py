@@ -4,7 +4,7 @@ Inputs/outputs are bf16 bit patterns (uint16 arrays); cos/sin tables float32.
 The reference fusions compute in fp32 and round once when storing; these
 functions do the same, in the order the reference kernels write it, so a
 correct GPU kernel lands within 1 bf16 ulp (the reduction order of the row sum
-is the only freedom). The BASELINE-only ops without a reference kernel
+is the only freedom). The benchmark-only ops without a reference kernel
 (modulate, gated residual, GELU-tanh) are evaluated in float64 and rounded once.
 """
 

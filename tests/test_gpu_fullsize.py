@@ -1,4 +1,4 @@
-"""Parity at the BASELINE sizes (480p-5s, and 768p-15s, the largest), where the CPU oracle
+"""Parity at the benchmark sizes (480p-5s, and 768p-15s, the largest), where the CPU oracle
 is too slow.
 
 The checks use properties that hold at any size:

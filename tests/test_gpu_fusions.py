@@ -118,7 +118,7 @@ def test_adaln_ops_random(rows, cols, n_table, n_index):
 
 
 def test_modulate_with_vectors_and_strided_rows():
-    """BASELINE form: [d] shift/scale vectors; activations as a strided row view."""
+    """Benchmark form: [d] shift/scale vectors; activations as a strided row view."""
 
     from h3_flash_b200.runtime.kernels import fusions as F
 

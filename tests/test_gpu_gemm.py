@@ -7,7 +7,7 @@ y in fp32 up to its one rounding at the store, so the bar is 1 bf16 ulp of the f
 result, except where a result is far smaller than its row (a sum that cancels): there
 the fp32 accumulation order alone moves it by a few fp32 ulps of the row's scale, and
 the bar is 2^-16 of the row's largest |y|. Shapes cover row tails (1, 257, 1000 rows),
-strided x and output rows, no bias, and the FFN shapes of the BASELINE block.
+strided x and output rows, no bias, and the FFN shapes of the benchmark block.
 """
 
 from __future__ import annotations

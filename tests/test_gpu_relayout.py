@@ -64,7 +64,7 @@ def test_fused_qknorm_rope_pack(rows, heads, world, rot):
 
 
 def test_pack_then_merge_roundtrip_is_identity():
-    """Size-independent property at a BASELINE-like shape: merging the pack's v part
+    """Size-independent property at a benchmark-like shape: merging the pack's v part
     back returns the original heads bit for bit."""
 
     from h3_flash_b200.runtime.parallel.relayout import merge_heads, pack_qkv_destination_major
